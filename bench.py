@@ -1,0 +1,343 @@
+"""Benchmark of the MaxSim hot path on B200 (one process per GPU).
+
+Default workload ("multi-query rerank"): per GPU a shard of 100,000 ragged
+documents, N_d ~ U[64, 300] (about 18.2M tokens, one concatenated fp16 token matrix + int64
+offsets), d = 128, L2-normalised Gaussian vectors; 64 queries x 32 tokens; each step scores every
+query against the shard (tcgen05 kernel), takes the per-query top-1000 and, at N > 1 GPUs, merges
+the per-shard top-1000 lists with one NCCL all-gather. Per-GPU work is fixed (weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3_256|c3_768|c5]
+    python bench.py --impl reference ...   # the reference algorithm on the host CPU cores
+
+Prints ONE JSON line on rank 0. ``value`` = doc-tokens scored per second over all GPUs
+(query x document-token pairs, B_q * T / t, the unit of the reference's throughput tables), timed
+on the device with CUDA events, max over ranks, inputs resident in HBM. ``e2e`` is the same metric
+through the public API with the queries copied from pinned host memory and the top-k results
+copied back every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (n_queries, nq, d, n_docs per GPU, nd_lo, nd_hi, k)
+    "c2": (64, 32, 128, 100_000, 64, 300, 1000),
+    "c1": (1, 32, 128, 1_000, 180, 180, 10),
+    "c3_256": (16, 32, 256, 50_000, 256, 256, 1000),
+    "c3_768": (16, 32, 768, 50_000, 256, 256, 1000),
+    "c5": (256, 32, 128, 1_250_000, 96, 160, 100),  # one eighth of the 10M-doc sharded corpus
+}
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every 200 ms while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device: torch.device):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception:  # NVML missing: report no clock record
+            self._h = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                r = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.reasons.update(v for k, v in self.REASONS.items() if r & k)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self) -> dict | None:
+        if self._h is None or not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": sorted(self.reasons)}
+
+
+# ------------------------------------------------------------------------------------ workload
+def make_corpus(n_docs: int, lo: int, hi: int, d: int, seed: int, device: torch.device):
+    lengths = np.random.default_rng(seed).integers(lo, hi + 1, n_docs).astype(np.int64)
+    off = np.zeros(n_docs + 1, dtype=np.int64)
+    np.cumsum(lengths, out=off[1:])
+    T = int(off[-1])
+    D = torch.empty(T, d, dtype=torch.float16, device=device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    step = 1 << 22
+    for t0 in range(0, T, step):  # N(0,1) in fp32, L2-normalised per token, fp16
+        x = torch.randn(min(step, T - t0), d, device=device, generator=g)
+        D[t0:t0 + x.shape[0]] = torch.nn.functional.normalize(x, dim=-1).half()
+    return D, torch.from_numpy(off).to(device), T
+
+
+def make_queries(nqry: int, nq: int, d: int, seed: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(nqry, nq, d, generator=g)
+    return torch.nn.functional.normalize(q, dim=-1).half()
+
+
+# ------------------------------------------------------------------------------------ arms
+def cpu_baseline(cfg, seconds: float = 12.0) -> dict:
+    """The reference algorithm (oracle port, NumPy fp32 einsum -> max -> sum, all host cores) on a
+    bounded sample: 1 query against the first documents of the shard."""
+    from oracle import maxsim_oracle as O
+    nqry, nq, d, n_docs, lo, hi, k = cfg
+    n_s = min(n_docs, 5000)
+    lengths = np.random.default_rng(42).integers(lo, hi + 1, n_s).astype(np.int64)
+    off = np.zeros(n_s + 1, np.int64)
+    np.cumsum(lengths, out=off[1:])
+    rng = np.random.default_rng(1)
+    D = rng.standard_normal((int(off[-1]), d), dtype=np.float32)
+    D /= np.linalg.norm(D, axis=1, keepdims=True)
+    D = D.astype(np.float16)
+    Q = make_queries(1, nq, d, 42)[0]
+    O.maxsim_ragged(Q, D, off)  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        O.maxsim_ragged(Q, D, off)
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": reps and int(off[-1]) / dt, "unit": "doc-tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 query x {n_s} ragged docs ({int(off[-1])} tokens, d={d}) x {reps} reps, "
+                      f"NumPy fp32 restatement of pytorch_maxsim_naive (oracle/maxsim_oracle.py)"}
+
+
+def run_reference(args, cfg, rank: int) -> None:
+    if rank != 0:
+        return
+    from oracle import maxsim_oracle as O
+    nqry, nq, d, n_docs, lo, hi, k = cfg
+    n_s = min(n_docs, 3000)
+    lengths = np.random.default_rng(42).integers(lo, hi + 1, n_s).astype(np.int64)
+    off = np.zeros(n_s + 1, np.int64)
+    np.cumsum(lengths, out=off[1:])
+    rng = np.random.default_rng(1)
+    D = rng.standard_normal((int(off[-1]), d), dtype=np.float32)
+    D = (D / np.linalg.norm(D, axis=1, keepdims=True)).astype(np.float16)
+    Q = make_queries(1, nq, d, 42)[0]
+    for _ in range(args.warmup):
+        s = O.maxsim_ragged(Q, D, off)
+        O.topk(s, min(k, n_s))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s = O.maxsim_ragged(Q, D, off)
+        O.topk(s, min(k, n_s))
+    dt = (time.perf_counter() - t0) / args.steps
+    val = int(off[-1]) / dt
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    sample = (f"per step 1 query x {n_s} ragged docs ({int(off[-1])} tokens, d={d}) + top-{min(k, n_s)}, "
+              "NumPy fp32 restatement of the reference's pytorch_maxsim_naive on all host cores")
+    print(json.dumps({
+        "impl": "reference", "metric": "doc-tokens scored/s", "value": val, "unit": "doc-tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, cfg),
+        "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "doc-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0}))
+
+
+def config_dict(args, cfg) -> dict:
+    nqry, nq, d, n_docs, lo, hi, k = cfg
+    return {"workload": f"{args.config}: {nqry} queries x {nq} tokens vs {n_docs} ragged docs per GPU "
+                        f"(N_d ~ U[{lo},{hi}], d={d}, fp16), top-{k}",
+            "n_queries": nqry, "nq": nq, "d": d, "docs_per_gpu": n_docs, "nd_range": [lo, hi], "k": k,
+            "parallelism": f"corpus-sharded x{args.gpus}, NCCL all-gather of per-shard top-k",
+            "l2": "inputs larger than L2 (corpus >> 126 MB)" if n_docs * (lo + hi) / 2 * d * 2 > 126e6
+                  else "corpus fits in L2"}
+
+
+def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
+    import tilemaxsim_b200 as tms
+    from tilemaxsim_b200 import _lib
+    from tilemaxsim_b200.sharded import ShardedIndex
+    nqry, nq, d, n_docs, lo, hi, k = cfg
+    D, off, T = make_corpus(n_docs, lo, hi, d, seed=42 + rank, device=device)
+    Qh = make_queries(nqry, nq, d, 7).pin_memory()
+    Qd = Qh.to(device)
+    index = ShardedIndex(D, off, doc_id_base=rank * n_docs, group=dist.group.WORLD if world > 1 else None)
+    torch.cuda.synchronize()
+
+    def step(Q):
+        return index.search(Q, k)
+
+    dense_ev = []
+
+    def step_timed(Q):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        scores = tms.maxsim_batched(Q, D, off)
+        e1.record()
+        dense_ev.append((e0, e1))
+        return index.search_scores(scores, k)
+
+    for _ in range(args.warmup):
+        step_timed(Qd)
+    torch.cuda.synchronize()
+    dense_ev.clear()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step_timed(Qd)
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    dense_ms = sum(a.elapsed_time(b) for a, b in dense_ev) / len(dense_ev)
+
+    # e2e: public API with host queries in pinned memory and results copied back, every step
+    for _ in range(max(1, args.warmup // 2)):
+        v, i = step(Qh.to(device, non_blocking=True))
+        v.cpu(), i.cpu()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        v, i = step(Qh.to(device, non_blocking=True))
+        vh, ih = v.to("cpu"), i.to("cpu")
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+
+    t_all = torch.tensor([ms, e2e_ms, dense_ms, float(T)], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = t_all.clone()
+        dist.all_reduce(mx[:3], op=dist.ReduceOp.MAX)
+        tot = t_all[3:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        t_all = torch.cat([mx[:3], tot])
+    ms, e2e_ms, dense_ms, T_total = t_all.tolist()
+    if rank != 0:
+        return
+
+    pairs = nqry * T_total
+    value = pairs / (ms * 1e-3)
+    pk = peaks()
+    flops_launch = 2.0 * nqry * nq * (T_total / world) * d
+    bytes_launch = (T_total / world) * d * 2 + nqry * nq * d * 2 + nqry * n_docs * 4 + (n_docs + 1) * 8
+    tensor_bound = nqry * nq >= 256
+    if tensor_bound:
+        ach = flops_launch / (dense_ms * 1e-3) / 1e12
+        peak, unit = pk["bf16_tflops_sustained"], "TFLOP/s"
+    else:
+        ach = bytes_launch / (dense_ms * 1e-3) / 1e9
+        peak, unit = pk["hbm_gbs"], "GB/s"
+    traffic = None
+    tf = ROOT / "profiles" / f"dense_maxsim_{args.config}_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    launches_per_step = 3 + (1 if world > 1 else 0) + (1 if nq > 32 else 0)
+    out = {
+        "metric": "doc-tokens scored/s", "value": value, "unit": "doc-tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": config_dict(args, cfg),
+        "queries_per_s": nqry / (ms * 1e-3),
+        "corpus_tokens_per_s": T_total / (ms * 1e-3),
+        "dense_kernel_ms": dense_ms,
+        "dense_hbm_gbs": bytes_launch / (dense_ms * 1e-3) / 1e9,
+        "dense_tflops": flops_launch / (dense_ms * 1e-3) / 1e12,
+        "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": ach, "peak": peak, "unit": unit,
+                     "frac": ach / peak, "traffic": traffic,
+                     "peak_src": f"{pk['src']} ({'bf16_tflops_sustained' if tensor_bound else 'hbm_gbs'})",
+                     "algorithmic": {"flops_per_launch": flops_launch, "bytes_per_launch": bytes_launch}},
+        "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s",
+                "h2d_bytes_per_step": Qh.numel() * Qh.element_size(),
+                "d2h_bytes_per_step": nqry * k * (4 + 8), "ms_per_step": e2e_ms},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(cfg)
+    print(json.dumps(out), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return 0
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    try:
+        run_ours(args, cfg, rank, world, device)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

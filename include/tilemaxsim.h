@@ -1,0 +1,127 @@
+/*
+ * tilemaxsim.h -- C ABI of libtilemaxsim_b200.so, the B200 (sm_100a) MaxSim scoring library.
+ *
+ * Late-interaction MaxSim:  score(q, doc) = sum_i max_j <Q[q,i,:], D[doc,j,:]>
+ *
+ * Every entry point is stream-ordered and asynchronous on `stream` (a cudaStream_t passed as
+ * void*), never allocates or frees device memory, and never synchronises the host. The caller
+ * owns every buffer, including outputs and workspace. All pointers are device pointers unless
+ * a comment says otherwise. Return value: TMS_OK or a TMS_ERR_* code (see tms_strerror).
+ *
+ * Reference interfaces replaced (ashutoshuiuc/tilemaxsim, paths inside that project):
+ *   tms_dense_maxsim   <- src/flash_maxsim_v2.py:227-289 flash_maxsim_v2_multiquery (kernels :73-190),
+ *                         src/flash_maxsim_v2.py:193-224 flash_maxsim_v2 (kernel :19-70),
+ *                         src/flash_maxsim_kernel.py:167-273 flash_maxsim_single / _batch / _multi_doc
+ *                         (kernels :25-164; TMS_OUT_TOKEN_MAX is the V1 per-query-token output)
+ *   tms_pq_table       <- src/flash_pqsim_kernel.py:190-211 TileMaxSimPQ.build_distance_table (kernel :31-67)
+ *   tms_pq_maxsim      <- src/flash_pqsim_kernel.py:213-280 TileMaxSimPQ.score_batch / score_single
+ *                         (kernels :70-173)
+ *   tms_topk           <- torch.topk after scoring, src/cycle3_experiments.py:215 (with ids_in it
+ *                         also merges per-shard top-k lists; the reference has no sharded search)
+ */
+#ifndef TILEMAXSIM_B200_H
+#define TILEMAXSIM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TMS_API __attribute__((visibility("default")))
+#else
+#define TMS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define TMS_OK 0
+#define TMS_ERR_INVALID 1     /* bad argument: shape, null pointer, misalignment */
+#define TMS_ERR_UNSUPPORTED 2 /* valid but not implemented (e.g. d not a multiple of 8) */
+#define TMS_ERR_CUDA 3        /* a CUDA runtime/driver call failed */
+#define TMS_ERR_TIMEOUT 4     /* a bounded device-side wait gave up (reported by tms_last_device_error) */
+#define TMS_ERR_WORKSPACE 5   /* workspace smaller than the *_workspace_size query */
+
+/* element types */
+#define TMS_F16 0
+#define TMS_BF16 1
+#define TMS_F32 2 /* multiplied as TF32 on the tensor cores, like the reference's tl.dot on fp32 */
+
+/* dense output modes */
+#define TMS_OUT_SCORE 0     /* out[q * n_docs + doc] = sum_i max_j <Q_qi, D_j>                 */
+#define TMS_OUT_TOKEN_MAX 1 /* out[(q * n_docs + doc) * nq + i] = max_j <Q_qi, D_j> (V1 output) */
+
+TMS_API const char* tms_strerror(int code);
+TMS_API const char* tms_version(void);
+
+/* Reads and clears the device-side error word (set by bounded waits that timed out). Synchronises
+ * `stream`. Returns TMS_OK or TMS_ERR_TIMEOUT; *detail (may be NULL) receives the raw word. */
+TMS_API int tms_last_device_error(void* stream, uint32_t* detail);
+
+/* ---------------------------------------------------------------- dense MaxSim (tcgen05 + TMA) */
+
+/* Workspace bytes tms_dense_maxsim needs for this problem (packed query tiles, and partial sums
+ * when nq > 32 in TMS_OUT_SCORE mode). */
+TMS_API size_t tms_dense_workspace_size(int dtype, int64_t n_queries, int64_t nq, int64_t d,
+                                int64_t n_docs, int out_mode);
+
+/* Q: (n_queries, nq, d) contiguous, dtype.
+ * D: (n_tokens, d) contiguous, dtype: all documents' tokens concatenated.
+ * Documents: if doc_offsets != NULL, doc i owns tokens [doc_offsets[i], doc_offsets[i+1]) (int64,
+ *   n_docs+1 entries, non-decreasing, doc_offsets[n_docs] <= n_tokens; an empty document scores
+ *   -inf, as the reference's running max starts at -inf). Otherwise every document has
+ *   nd_uniform tokens and doc i owns [i*nd_uniform, (i+1)*nd_uniform) (the padded (B,Nd,d) layout:
+ *   every row participates, zero padding included).
+ * out: fp32, TMS_OUT_SCORE -> (n_queries, n_docs); TMS_OUT_TOKEN_MAX -> (n_queries, n_docs, nq).
+ * Requirements: d % 8 == 0 (16-bit) or d % 4 == 0 (fp32); Q, D 16-byte aligned; n_tokens < 2^31. */
+TMS_API int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int64_t nq, int64_t d,
+                     const void* D, int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
+                     int64_t nd_uniform, float* out, int out_mode, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- PQ asymmetric distance (ADC) */
+
+/* table[(q*nq + i) * M*K + m*K + k] = <Q[q,i, m*dsub:(m+1)*dsub], codebook[m,k,:]> in fp32.
+ * Q dtype: TMS_F16/BF16/F32; codebook dtype: TMS_F16/BF16/F32, (M, K, dsub) contiguous. */
+TMS_API int tms_pq_table(const void* Q, int q_dtype, int64_t n_queries, int64_t nq, const void* codebook,
+                 int cb_dtype, int64_t M, int64_t K, int64_t dsub, float* table, void* stream);
+
+TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K, int64_t n_docs);
+
+/* codes: (n_tokens, M) uint8, doc layout as in tms_dense_maxsim (offsets or nd_uniform).
+ * out[q * n_docs + doc] = sum_i max_j sum_m table[q,i,m,codes[j,m]]; the distance table is built in
+ * shared memory from Q and the codebook inside the kernel (K <= 256). */
+TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq, const void* codebook,
+                  int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
+                  int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                  float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- top-k */
+
+TMS_API size_t tms_topk_workspace_size(int64_t rows, int64_t n, int64_t k);
+
+/* Per row r of scores (rows, n) fp32 with row stride ld: the k best (score descending, then id
+ * ascending; NaN ranks last) -> out_vals (rows, k), out_ids (rows, k) int64. The id of column c is
+ * ids_in[r*ld_ids + c] when ids_in != NULL, else c + id_base. k <= 2048 and k <= n. */
+TMS_API int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, int64_t k,
+             const int64_t* ids_in, int64_t ld_ids, int64_t id_base, float* out_vals,
+             int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- introspection and test hooks */
+
+/* Launch plan the dense kernel would use (no reference counterpart): info[0..9] = tokens per tile,
+ * query-resident flag, query tiles per CTA group, pipeline stages, groups, token ranges, query
+ * tiles, 128-byte K chunks, dynamic shared memory bytes, CTAs. */
+TMS_API int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs,
+                                int64_t n_tokens, int out_mode, int num_sms, int64_t* info);
+
+/* Test hook (no reference counterpart): wait limit of the bounded device waits in ns (0 keeps the
+ * current limit) and fault flags (bit 0: the dense kernel's producer issues no load, so the
+ * consumers' waits run out and tms_last_device_error reports TMS_ERR_TIMEOUT). */
+TMS_API void tms_set_debug(uint64_t timeout_ns, int flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TILEMAXSIM_B200_H */

@@ -1,0 +1,69 @@
+"""The CPU oracle against the golden outputs of the reference's own PyTorch functions."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import recipes as R
+from conftest import load_golden
+from oracle import maxsim_oracle as O
+
+
+@pytest.mark.parametrize("i", range(len(R.EXP10_CONFIGS)))
+def test_exp10_padded(i):
+    meta, g = load_golden(f"exp10_{i}")
+    c = R.exp10_case(i)
+    assert R.sha256(c["Q"], c["D"]) == meta["sha256"], "input recipe drifted from the fixture"
+    np.testing.assert_allclose(O.maxsim_padded(c["Q"], c["D"]), g["scores"], rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(O.token_max_padded(c["Q"], c["D"]), g["token_max"], rtol=1e-5, atol=1e-5)
+
+
+def test_v1_selfcheck_naive_equals_loop():
+    meta, g = load_golden("v1_selfcheck")
+    c = R.v1_selfcheck_case()
+    assert R.sha256(c["Q"], c["D"]) == meta["sha256"]
+    np.testing.assert_allclose(O.maxsim_padded(c["Q"], c["D"]), g["naive"], rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(g["loop"], g["naive"], rtol=1e-5, atol=1e-4)
+
+
+RAGGED = {"ragged_f16": {}, "ragged_bf16": {"dtype": torch.bfloat16, "seed": 11},
+          "ragged_nq20": {"nq": 20, "n_queries": 2, "seed": 13},
+          "ragged_nq40": {"nq": 40, "n_queries": 2, "n_docs": 120, "seed": 17}}
+
+
+@pytest.mark.parametrize("name", list(RAGGED))
+def test_ragged(name):
+    meta, g = load_golden(name)
+    c = R.ragged_case(**RAGGED[name])
+    assert R.sha256(c["Qb"], c["D"], c["offsets"].numpy()) == meta["sha256"]
+    s = O.maxsim_ragged(c["Qb"], c["D"], c["offsets"].numpy(), chunk_docs=37)
+    assert np.isneginf(g["scores"]).sum() >= 3 * c["Qb"].shape[0]  # the forced empty documents
+    np.testing.assert_allclose(s, g["scores"], rtol=1e-5, atol=1e-4)
+    tm = O.token_max_ragged(c["Qb"], c["D"], c["offsets"].numpy())
+    np.testing.assert_allclose(tm, g["token_max"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name,cb_dtype", [("pq_f32", torch.float32), ("pq_f16", torch.float16)])
+def test_pq(name, cb_dtype):
+    meta, g = load_golden(name)
+    c = R.pq_case(cb_dtype)
+    assert R.sha256(c["codebook"], c["Q"], c["codes"]) == meta["sha256"]
+    np.testing.assert_allclose(O.pq_maxsim_adc(c["Q"], c["codebook"], c["codes"]), g["adc"], rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(O.pq_maxsim_decompress(c["Q"], c["codebook"], c["codes"]), g["decompress"],
+                               rtol=1e-5, atol=1e-4)
+    # ragged ADC form on the same codes (every doc the same length) agrees with the padded form
+    B, Nd, M = c["codes"].shape
+    off = np.arange(B + 1, dtype=np.int64) * Nd
+    r = O.pq_maxsim_adc_ragged(c["Q"][None], c["codebook"], c["codes"].reshape(B * Nd, M), off)[0]
+    np.testing.assert_allclose(r, g["adc"], rtol=1e-5, atol=1e-4)
+
+
+def test_topk_ties():
+    meta, g = load_golden("topk_ties")
+    s = R.topk_case()["scores"]
+    assert R.sha256(s) == meta["sha256"]
+    vals, ids = O.topk(s, 1000)
+    np.testing.assert_array_equal(ids, g["order"])
+    np.testing.assert_array_equal(vals[:, :100][~np.isnan(vals[:, :100])],
+                                  g["torch_topk_values"][~np.isnan(vals[:, :100])])

@@ -1,0 +1,84 @@
+"""Top-k (tms_topk) and PQ-ADC (tms_pq_table, tms_pq_maxsim) kernels against the oracle and the
+reference's golden outputs. Top-k ids must be identical (score descending, id ascending); PQ scores
+within 1e-3 relative of the reference's ADC path."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import recipes as R
+from conftest import load_golden
+from oracle import maxsim_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def test_topk_ties_golden(cuda_device):
+    from tilemaxsim_b200 import topk
+    _, g = load_golden("topk_ties")
+    s = R.topk_case()["scores"].to(cuda_device)
+    for k in (1, 10, 100, 1000):
+        vals, ids = topk(s, k)
+        np.testing.assert_array_equal(ids.cpu().numpy(), g["order"][:, :k])
+        want, _ = O.topk(s.cpu(), k)
+        np.testing.assert_array_equal(vals.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows,n,k", [(3, 100_000, 1000), (64, 100_000, 1000), (2, 20_000, 10),
+                                      (1, 1_250_003, 100), (5, 16_385, 2048), (4, 7, 7)])
+def test_topk_random(rows, n, k, cuda_device):
+    from tilemaxsim_b200 import topk
+    g = torch.Generator().manual_seed(rows * n + k)
+    s = torch.randn(rows, n, generator=g)
+    s[:, ::97] = s[:, :1]  # exact ties across the row
+    vals, ids = topk(s.to(cuda_device), k, id_base=5)
+    wv, wi = O.topk(s, k)
+    np.testing.assert_array_equal(ids.cpu().numpy(), wi + 5)
+    np.testing.assert_array_equal(vals.cpu().numpy(), wv)
+
+
+def test_topk_merge_with_ids(cuda_device):
+    from tilemaxsim_b200 import topk
+    g = torch.Generator().manual_seed(1)
+    s = torch.randn(6, 8 * 100, generator=g).round(decimals=1)
+    ids = torch.randperm(10_000, generator=g)[: 6 * 800].reshape(6, 800)
+    vals, out = topk(s.to(cuda_device), 100, ids=ids.to(cuda_device))
+    wv, wi = O.topk(s, 100, ids=ids.numpy())
+    np.testing.assert_array_equal(out.cpu().numpy(), wi)
+    np.testing.assert_array_equal(vals.cpu().numpy(), wv)
+
+
+@pytest.mark.parametrize("name,cb_dtype", [("pq_f32", torch.float32), ("pq_f16", torch.float16)])
+def test_pq_golden(name, cb_dtype, cuda_device):
+    from tilemaxsim_b200 import TileMaxSimPQ
+    _, g = load_golden(name)
+    c = R.pq_case(cb_dtype)
+    pq = TileMaxSimPQ(c["codebook"].to(cuda_device))
+    Q, codes = c["Q"].to(cuda_device), c["codes"].to(cuda_device)
+    got = pq.score_batch(Q, codes).cpu().numpy()
+    np.testing.assert_allclose(got, g["adc"], rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(got, g["decompress"], rtol=1e-3, atol=1e-3)
+    s1 = pq.score_single(Q, codes[3])
+    assert s1.dim() == 0
+    np.testing.assert_allclose(s1.item(), g["adc"][3], rtol=1e-3, atol=1e-3)
+    T = pq.build_distance_table(Q).cpu().numpy()
+    np.testing.assert_allclose(T, O.pq_table(c["Q"], c["codebook"]), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("M,K,dsub,nq", [(16, 256, 8, 32), (8, 256, 16, 32), (32, 256, 4, 32),
+                                         (16, 100, 8, 5), (12, 256, 8, 40)])
+def test_pq_ragged_multiquery(M, K, dsub, nq, cuda_device):
+    from tilemaxsim_b200 import TileMaxSimPQ
+    lengths = R.ragged_lengths(400, 0, 200, seed=M + K)
+    off = R.offsets_from_lengths(lengths)
+    cb = R.randn((M, K, dsub), 3, torch.float32)
+    Qb = R.normalized((3, nq, M * dsub), 4)
+    codes = torch.randint(0, K, (int(off[-1]), M), generator=R.gen(5), dtype=torch.uint8)
+    pq = TileMaxSimPQ(cb.to(cuda_device))
+    got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device), torch.from_numpy(off).to(cuda_device))
+    want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
+    got = got.cpu().numpy()
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)

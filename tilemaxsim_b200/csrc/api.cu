@@ -1,0 +1,144 @@
+// api.cu -- library-wide host pieces of the C ABI: status strings, the per-device error word,
+// device facts, TMA descriptor encoding and the test hooks.
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "tms_internal.h"
+
+namespace tms {
+
+// One error word per device that loads the library; bounded waits that give up write here.
+__device__ uint32_t g_tms_dev_error_word;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_dev_mutex;
+
+uint64_t g_timeout_ns = 2000000000ull;  // 2 s
+int g_debug_flags = 0;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+const DeviceInfo* current_device_info(int* status) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *status = TMS_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& d = g_devices[dev];
+  if (d.device != dev) {
+    DeviceInfo n;
+    n.device = dev;
+    if (cudaDeviceGetAttribute(&n.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+            cudaSuccess) {
+      *status = TMS_ERR_CUDA;
+      return nullptr;
+    }
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tms_dev_error_word) != cudaSuccess) {
+      *status = TMS_ERR_CUDA;
+      return nullptr;
+    }
+    n.err_word = static_cast<uint32_t*>(p);
+    d = n;
+  }
+  *status = TMS_OK;
+  return &d;
+}
+
+uint64_t wait_timeout_ns() { return g_timeout_ns; }
+int debug_flags() { return g_debug_flags; }
+
+long env_int(const char* name, long fallback) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return fallback;
+  char* end = nullptr;
+  const long x = std::strtol(v, &end, 10);
+  return (end && *end == '\0') ? x : fallback;
+}
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                   uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return TMS_ERR_CUDA;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TMS_OK : TMS_ERR_CUDA;
+}
+
+}  // namespace tms
+
+using namespace tms;
+
+extern "C" const char* tms_strerror(int code) {
+  switch (code) {
+    case TMS_OK: return "ok";
+    case TMS_ERR_INVALID: return "invalid argument";
+    case TMS_ERR_UNSUPPORTED: return "unsupported shape or type";
+    case TMS_ERR_CUDA: return "CUDA error";
+    case TMS_ERR_TIMEOUT: return "device wait timed out";
+    case TMS_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown error";
+  }
+}
+
+extern "C" const char* tms_version(void) { return "tilemaxsim_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int tms_last_device_error(void* stream, uint32_t* detail) {
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t word = 0;
+  if (cudaMemcpyAsync(&word, dev->err_word, sizeof(word), cudaMemcpyDeviceToHost, st) !=
+      cudaSuccess)
+    return TMS_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return TMS_ERR_CUDA;
+  if (word != 0) {
+    const uint32_t zero = 0;
+    if (cudaMemcpyAsync(dev->err_word, &zero, sizeof(zero), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return TMS_ERR_CUDA;
+  }
+  if (detail) *detail = word;
+  return word ? TMS_ERR_TIMEOUT : TMS_OK;
+}
+
+// Test hook: wait limit for the bounded device waits (0 keeps the current value) and fault flags
+// (bit 0: the dense kernel's producer issues no load, so its consumers' waits run out).
+extern "C" void tms_set_debug(uint64_t timeout_ns, int flags) {
+  if (timeout_ns) g_timeout_ns = timeout_ns;
+  g_debug_flags = flags;
+}

@@ -1,0 +1,645 @@
+// dense_maxsim.cu -- fused MaxSim on the sm_100a tensor cores.
+//
+//   score[q, doc] = sum_i max_{j in doc} <Q[q,i,:], D[j,:]>
+//
+// Reference semantics: src/flash_maxsim_v2.py:73-130 (_flash_maxsim_v2_multiquery_kernel: query
+// block x doc tile dot, row max, running max, sum of the per-token maxima, query rows past Nq add
+// 0, doc rows past Nd are masked) and :133-190 (d > 128 accumulates partial dots over d before the
+// max); src/flash_maxsim_kernel.py:25-164 (V1: per-query-token maxima, running max starts at -inf
+// so an empty document gives -inf) and :248-273 (ragged documents through an offsets array).
+//
+// B200 design (not a translation of the Triton kernels):
+//  * Queries are packed into 128-row "M tiles": every query owns ceil(Nq/32) groups of 32 rows
+//    ("chunks"), so one warp's TMEM lane quarter holds exactly one query chunk. The MMA computes
+//    S = Qtile . Dtile^T with the query rows on TMEM lanes and doc tokens on TMEM columns.
+//  * Doc tokens are streamed as TN-token tiles (TN = 256 or 128) by TMA (128-byte swizzle) into a
+//    ring of shared-memory stages; each D byte is read from HBM once per CTA group.
+//  * One thread issues tcgen05.mma (kind::f16 for fp16/bf16, kind::tf32 for fp32 inputs) into a
+//    double-buffered fp32 accumulator in TMEM (2 x TN columns).
+//  * Four epilogue warps read their 32 lanes with tcgen05.ld and run a segmented max along the
+//    columns (doc boundaries are warp-uniform, taken from the offsets array), then one warp-shuffle
+//    sum over the 32 query-token lanes per finished document. The Nq x Nd similarity matrix never
+//    leaves the SM.
+//  * The CTA grid is (token range) x (query group). Token ranges are cut at document boundaries
+//    (warp-cooperative binary search on the offsets), so no document straddles two CTAs and no
+//    cross-CTA merge or atomic is needed: results are deterministic.
+//  * Q-resident mode keeps the CTA's G query tiles in shared memory for the whole range; streaming
+//    mode (large d) loads one (query chunk, doc chunk) pair per pipeline stage.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2..5 = epilogue (lane quarter = warp % 4).
+#include <cstdio>
+#include <cstdlib>
+
+#include "tms_device.cuh"
+#include "tms_internal.h"
+
+namespace tms {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kQTileRows = 128;
+constexpr uint32_t kQChunkBytes = kQTileRows * 128;  // one 128-row x 128-byte K chunk of Q
+constexpr float kNegInf = -__builtin_huge_valf();
+
+struct DenseArgs {
+  DocLayout docs;
+  float* out;
+  uint32_t* err;
+  uint64_t timeout_ns;
+  int n_chunks_total;  // 32-row query chunks over all queries
+  int nchunk;          // chunks per query
+  int nq;
+  int n_mtiles;
+  int G;         // M tiles per CTA group
+  int n_groups;  // CTA groups along the query dimension
+  int n_ranges;  // token ranges along the document dimension
+  int kc;        // 128-byte K chunks per row (ceil(d * esize / 128))
+  int stages;
+  int out_mode;
+  uint32_t ab_format;  // MMA operand format: 0 = f16, 1 = bf16, 2 = tf32
+  int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits)
+};
+
+// Shared-memory carve-up, identical on host and device.
+struct SmemLayout {
+  uint32_t q_off, stage_off, stage_bytes, bar_off, carry_off, misc_off, total;
+};
+__host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G, int kc,
+                                                        int stages) {
+  SmemLayout L;
+  L.q_off = 0;
+  const uint32_t q_bytes = qres ? static_cast<uint32_t>(G * kc) * kQChunkBytes : 0u;
+  L.stage_off = q_bytes;
+  L.stage_bytes = qres ? static_cast<uint32_t>(kc * TN * 128) : (kQChunkBytes + TN * 128u);
+  L.bar_off = L.stage_off + static_cast<uint32_t>(stages) * L.stage_bytes;
+  const uint32_t n_bars = 2u * stages + 6u;
+  L.carry_off = (L.bar_off + n_bars * 8u + 15u) & ~15u;
+  L.misc_off = L.carry_off + static_cast<uint32_t>(G) * kQTileRows * 4u;
+  L.total = L.misc_off + 64u + 1024u;  // + slack to align the dynamic base to 1024
+  return L;
+}
+
+struct RangeInfo {
+  int64_t doc_lo, doc_hi, tok_lo, tok_hi;
+};
+
+// Max over v[lo, hi) (empty -> -inf).
+__device__ __forceinline__ float range_max(const float (&v)[32], int lo, int hi) {
+  if (lo == 0 && hi == 32) {
+    float m0 = fmaxf(v[0], v[1]), m1 = fmaxf(v[2], v[3]), m2 = fmaxf(v[4], v[5]),
+          m3 = fmaxf(v[6], v[7]);
+#pragma unroll
+    for (int i = 8; i < 32; i += 8) {
+      m0 = fmaxf(m0, fmaxf(v[i + 0], v[i + 1]));
+      m1 = fmaxf(m1, fmaxf(v[i + 2], v[i + 3]));
+      m2 = fmaxf(m2, fmaxf(v[i + 4], v[i + 5]));
+      m3 = fmaxf(m3, fmaxf(v[i + 6], v[i + 7]));
+    }
+    return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+  }
+  float m = kNegInf;
+  const uint32_t span = static_cast<uint32_t>(hi - lo);
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (static_cast<uint32_t>(i - lo) < span) m = fmaxf(m, v[i]);
+  return m;
+}
+
+template <int TN, bool QRES, bool TF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
+                        const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t q_s = sbase + L.q_off;
+  const uint32_t st_s = sbase + L.stage_off;
+  const uint32_t bar_s = sbase + L.bar_off;
+  const int S = a.stages;
+  auto full_bar = [&](int s) { return bar_s + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_s + 8u * (S + s); };
+  auto accf_bar = [&](int b) { return bar_s + 8u * (2 * S + b); };
+  auto acce_bar = [&](int b) { return bar_s + 8u * (2 * S + 2 + b); };
+  const uint32_t qfull_bar = bar_s + 8u * (2 * S + 4);
+  const uint32_t done_bar = bar_s + 8u * (2 * S + 5);
+  float* carry = reinterpret_cast<float*>(smem + L.carry_off);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+  RangeInfo* rinfo = reinterpret_cast<RangeInfo*>(smem + L.misc_off + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int range = blockIdx.x / a.n_groups;
+  const int group = blockIdx.x - range * a.n_groups;
+  const int m_first = group * a.G;
+  const int g_this = min(a.G, a.n_mtiles - m_first);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 4);
+    }
+    mbar_init(qfull_bar, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    // Cut this CTA's token range at document boundaries.
+    const int64_t t_first = a.docs.start(0);
+    const int64_t t_last = a.docs.start(a.docs.n_docs);
+    const int64_t span = t_last - t_first;
+    const int64_t tgt_lo = t_first + span * range / a.n_ranges;
+    const int64_t tgt_hi = t_first + span * (range + 1) / a.n_ranges;
+    const int64_t doc_lo = (range == 0) ? 0 : warp_lower_bound(a.docs, tgt_lo);
+    const int64_t doc_hi =
+        (range == a.n_ranges - 1) ? a.docs.n_docs : warp_lower_bound(a.docs, tgt_hi);
+    if (lane == 0) {
+      rinfo->doc_lo = doc_lo;
+      rinfo->doc_hi = doc_hi;
+      rinfo->tok_lo = a.docs.start(doc_lo);
+      rinfo->tok_hi = (doc_hi > doc_lo) ? a.docs.start(doc_hi) : a.docs.start(doc_lo);
+      prefetch_tmap(&dmap);
+      prefetch_tmap(&qmap);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 2 * TN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = *tmem_slot;
+  const int64_t doc_lo = rinfo->doc_lo, doc_hi = rinfo->doc_hi;
+  const int64_t tok_lo = rinfo->tok_lo, tok_hi = rinfo->tok_hi;
+  const uint64_t tmo = a.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && !(a.debug_flags & 1)) {
+      const uint64_t pol_d = (a.n_groups > 1) ? policy_evict_normal() : policy_evict_first();
+      const uint64_t pol_q = policy_evict_last();
+      const int cw = TF32 ? 32 : 64;  // elements per 128-byte chunk
+      if (QRES && tok_hi > tok_lo) {
+        mbar_arrive_expect_tx(qfull_bar, static_cast<uint32_t>(g_this * a.kc) * kQChunkBytes);
+        for (int m = 0; m < g_this; ++m)
+          for (int c = 0; c < a.kc; ++c)
+            tma_load_2d(q_s + static_cast<uint32_t>(m * a.kc + c) * kQChunkBytes, &qmap, qfull_bar,
+                        c * cw, (m_first + m) * kQTileRows, pol_q);
+      }
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+        if (QRES) {
+          if (!(ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 1))) break;
+          mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(a.kc * TN * 128));
+          const uint32_t st = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
+          for (int c = 0; c < a.kc; ++c)
+            tma_load_2d(st + static_cast<uint32_t>(c * TN * 128), &dmap, full_bar(s), c * cw,
+                        static_cast<int32_t>(t0), pol_d);
+          if (++s == S) { s = 0; ph ^= 1u; }
+        } else {
+          for (int m = 0; ok && m < g_this; ++m) {
+            for (int c = 0; c < a.kc; ++c) {
+              if (!(ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 2))) break;
+              mbar_arrive_expect_tx(full_bar(s), kQChunkBytes + TN * 128u);
+              const uint32_t st = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
+              tma_load_2d(st, &qmap, full_bar(s), c * cw, (m_first + m) * kQTileRows, pol_q);
+              tma_load_2d(st + kQChunkBytes, &dmap, full_bar(s), c * cw, static_cast<int32_t>(t0),
+                          pol_d);
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(128, TN, a.ab_format);
+      bool ok = true;
+      if (QRES && tok_hi > tok_lo) ok = mbar_wait(qfull_bar, 0, abort_flag, tmo, a.err, 3);
+      int s = 0;
+      uint32_t ph = 0, u = 0;
+      for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+        if (QRES) {
+          if (!(ok = mbar_wait(full_bar(s), ph, abort_flag, tmo, a.err, 4))) break;
+          tc_fence_after();
+        }
+        for (int m = 0; ok && m < g_this; ++m, ++u) {
+          const uint32_t slot = u & 1u;
+          if (!(ok = mbar_wait(acce_bar(slot), ((u >> 1) & 1u) ^ 1u, abort_flag, tmo, a.err, 5)))
+            break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + slot * TN;
+          for (int c = 0; c < a.kc; ++c) {
+            uint32_t a_base, b_base;
+            if (QRES) {
+              a_base = q_s + static_cast<uint32_t>(m * a.kc + c) * kQChunkBytes;
+              b_base = st_s + static_cast<uint32_t>(s) * L.stage_bytes +
+                       static_cast<uint32_t>(c * TN * 128);
+            } else {
+              if (!(ok = mbar_wait(full_bar(s), ph, abort_flag, tmo, a.err, 6))) break;
+              tc_fence_after();
+              a_base = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
+              b_base = a_base + kQChunkBytes;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = sw128_kmajor_desc(a_base + 32u * k);
+              const uint64_t bd = sw128_kmajor_desc(b_base + 32u * k);
+              if (TF32)
+                mma_tf32(d_tmem, ad, bd, idesc, (c | k) != 0);
+              else
+                mma_f16(d_tmem, ad, bd, idesc, (c | k) != 0);
+            }
+            if (!QRES) {
+              mma_commit(empty_bar(s));
+              if (++s == S) { s = 0; ph ^= 1u; }
+            }
+          }
+          if (!ok) break;
+          mma_commit(accf_bar(slot));
+        }
+        if (QRES && ok) {
+          mma_commit(empty_bar(s));
+          if (++s == S) { s = 0; ph ^= 1u; }
+        }
+      }
+      // Make sure every MMA this thread issued has landed before TMEM is released.
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0, abort_flag, tmo, a.err, 7);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int lg = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = lg * 32 + lane;
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(lg * 32) << 16);
+    for (int m = 0; m < g_this; ++m) carry[m * kQTileRows + row] = kNegInf;
+    const DocLayout docs = a.docs;
+    auto doc_end = [&](int64_t dd) -> int64_t {
+      return dd < doc_hi ? docs.start(dd + 1) : INT64_MAX;
+    };
+    auto emit = [&](int chunk, int64_t dd, float rm) {
+      const int q = chunk / a.nchunk;
+      const int rq = (chunk - q * a.nchunk) * 32 + lane;
+      const bool valid = rq < a.nq;
+      if (a.out_mode == TMS_OUT_SCORE) {
+        const float s = warp_sum(valid ? rm : 0.0f);
+        if (lane == 0) a.out[static_cast<int64_t>(chunk) * docs.n_docs + dd] = s;
+      } else if (valid) {
+        a.out[(static_cast<int64_t>(q) * docs.n_docs + dd) * a.nq + rq] = rm;
+      }
+    };
+
+    int64_t doc = doc_lo;
+    int64_t dend = doc_end(doc);
+    uint32_t u = 0;
+    bool ok = true;
+    for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+      int64_t next_doc = doc, next_dend = dend;
+      for (int m = 0; m < g_this; ++m, ++u) {
+        const uint32_t slot = u & 1u;
+        int w = 0;
+        if (lane == 0) w = mbar_wait(accf_bar(slot), (u >> 1) & 1u, abort_flag, tmo, a.err, 8);
+        ok = __shfl_sync(0xffffffffu, w, 0) != 0;
+        if (!ok) break;
+        tc_fence_after();
+        const int chunk = (m_first + m) * 4 + lg;
+        if (chunk < a.n_chunks_total) {
+          float rm = carry[m * kQTileRows + row];
+          int64_t dd = doc, de = dend;
+#pragma unroll 1
+          for (int j = 0; j < TN / 32; ++j) {
+            const int64_t c0 = t0 + 32 * j;
+            if (c0 >= tok_hi) break;
+            float v[32];
+            tmem_ld32(t_lane + slot * TN + 32u * j, v);
+            const int n = (tok_hi - c0 < 32) ? static_cast<int>(tok_hi - c0) : 32;
+            int lo = 0;
+            while (true) {
+              const int hi = (de - c0 < n) ? static_cast<int>(de - c0) : n;
+              rm = fmaxf(rm, range_max(v, lo, hi));
+              if (de - c0 >= n) break;
+              emit(chunk, dd, rm);
+              rm = kNegInf;
+              ++dd;
+              de = doc_end(dd);
+              lo = hi;
+            }
+          }
+          carry[m * kQTileRows + row] = rm;
+          next_doc = dd;
+          next_dend = de;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar(slot));
+      }
+      doc = next_doc;
+      dend = next_dend;
+    }
+    if (ok) {
+      // Documents still open at the end of the range: the last one (ends at tok_hi) and any empty
+      // documents after it.
+      for (int m = 0; m < g_this; ++m) {
+        const int chunk = (m_first + m) * 4 + lg;
+        if (chunk >= a.n_chunks_total) continue;
+        float rm = carry[m * kQTileRows + row];
+        for (int64_t dd = doc; dd < doc_hi; ++dd) {
+          emit(chunk, dd, rm);
+          rm = kNegInf;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * TN);
+  }
+}
+
+// Packs Q (n_queries, nq, d) into 128-row M tiles: chunk c (32 rows) = rows [32p, 32p+32) of query
+// c / nchunk (p = c % nchunk); rows past nq and chunks past the last query are zero.
+__global__ void pack_query_tiles_kernel(const uint4* __restrict__ q, uint4* __restrict__ qp,
+                                        int64_t n_vec_total, int vec_per_row, int nq, int nchunk,
+                                        int n_chunks_total) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_vec_total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int v = static_cast<int>(i - r * vec_per_row);
+    const int64_t c = r >> 5;
+    const int ln = static_cast<int>(r & 31);
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (c < n_chunks_total) {
+      const int64_t qi = c / nchunk;
+      const int src = static_cast<int>(c - qi * nchunk) * 32 + ln;
+      if (src < nq) val = q[(qi * nq + src) * vec_per_row + v];
+    }
+    qp[i] = val;
+  }
+}
+
+// out[q, doc] = sum over the query's chunks, in chunk order (deterministic).
+__global__ void sum_query_chunks_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                        int64_t n_queries, int64_t n_docs, int nchunk) {
+  const int64_t total = n_queries * n_docs;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t q = i / n_docs;
+    const int64_t dd = i - q * n_docs;
+    float s = 0.0f;
+    for (int p = 0; p < nchunk; ++p) s += partial[(q * nchunk + p) * n_docs + dd];
+    out[i] = s;
+  }
+}
+
+__global__ void fill_kernel(float* out, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = v;
+}
+
+struct DensePlan {
+  int esize, cw, kc, nchunk, n_chunks_total, n_mtiles;
+  int TN, G, stages, n_groups, n_ranges;
+  bool qres;
+  size_t qp_bytes, partial_bytes;
+};
+
+int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs,
+               int64_t n_tokens, int out_mode, int num_sms, int max_smem, DensePlan* p) {
+  p->esize = (dtype == TMS_F32) ? 4 : 2;
+  p->cw = 128 / p->esize;
+  if ((d * p->esize) % 16 != 0) return TMS_ERR_UNSUPPORTED;
+  p->kc = static_cast<int>((d + p->cw - 1) / p->cw);
+  p->nchunk = static_cast<int>((nq + 31) / 32);
+  const int64_t chunks = n_queries * p->nchunk;
+  const int64_t mtiles = (chunks + 3) / 4;
+  if (chunks > (int64_t(1) << 30) || mtiles * kQTileRows > (int64_t(1) << 31) - 1)
+    return TMS_ERR_UNSUPPORTED;
+  p->n_chunks_total = static_cast<int>(chunks);
+  p->n_mtiles = static_cast<int>(mtiles);
+  p->qp_bytes = align_up(static_cast<size_t>(mtiles) * kQTileRows * d * p->esize, 1024);
+  p->partial_bytes = (out_mode == TMS_OUT_SCORE && p->nchunk > 1)
+                         ? align_up(static_cast<size_t>(chunks) * n_docs * 4, 256)
+                         : 0;
+
+  const int budget = max_smem - 2048 - 1024 - 64;
+  p->TN = static_cast<int>(env_int("TMS_DENSE_TN", p->kc <= 2 ? 256 : 128));
+  if (p->TN != 128 && p->TN != 256) p->TN = 256;
+  const int stage_d = p->kc * p->TN * 128;
+  const int qtile = p->kc * static_cast<int>(kQChunkBytes);
+  const bool force_stream = env_int("TMS_DENSE_STREAM", 0) != 0;
+  p->qres = !force_stream && (qtile + 2 * stage_d <= budget);
+  if (p->qres) {
+    int gmax = (budget - 2 * stage_d) / qtile;
+    gmax = static_cast<int>(env_int("TMS_DENSE_G", gmax < 4 ? gmax : 4));
+    if (gmax < 1) gmax = 1;
+    // Per-CTA time grows with G x ceil(n_mtiles / G) (units per tile x token share): take the
+    // group size that minimises it, the larger one on ties (fewer re-reads of each doc tile).
+    int g = 1;
+    int64_t best = p->n_mtiles;
+    for (int c = 2; c <= gmax && c <= p->n_mtiles; ++c) {
+      const int64_t cost = static_cast<int64_t>(c) * ((p->n_mtiles + c - 1) / c);
+      if (cost <= best) { best = cost; g = c; }
+    }
+    p->n_groups = (p->n_mtiles + g - 1) / g;
+    p->G = (p->n_mtiles + p->n_groups - 1) / p->n_groups;
+    int st = (budget - p->G * qtile) / stage_d;
+    st = st > 4 ? 4 : st;
+    p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
+  } else {
+    const int stage = static_cast<int>(kQChunkBytes) + p->TN * 128;
+    int g = p->n_mtiles < 4 ? p->n_mtiles : 4;
+    g = static_cast<int>(env_int("TMS_DENSE_G", g));
+    p->n_groups = (p->n_mtiles + g - 1) / g;
+    p->G = (p->n_mtiles + p->n_groups - 1) / p->n_groups;
+    int st = budget / stage;
+    st = st > 6 ? 6 : st;
+    p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
+  }
+  if (p->stages < 1) p->stages = 1;
+  const SmemLayout L = dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages);
+  if (static_cast<int>(L.total) > max_smem) return TMS_ERR_UNSUPPORTED;
+  int64_t ranges = p->n_groups >= num_sms ? 1 : num_sms / p->n_groups;
+  ranges = env_int("TMS_DENSE_RANGES", ranges);
+  const int64_t tiles = (n_tokens + p->TN - 1) / p->TN;
+  if (ranges > tiles) ranges = tiles;
+  if (ranges > n_docs) ranges = n_docs;
+  if (ranges < 1) ranges = 1;
+  p->n_ranges = static_cast<int>(ranges);
+  if (static_cast<int64_t>(p->n_ranges) * p->n_groups > 0x7fffffffLL) return TMS_ERR_UNSUPPORTED;
+  return TMS_OK;
+}
+
+template <int TN, bool QRES, bool TF32>
+int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
+                   const DensePlan& p, cudaStream_t st) {
+  auto kern = dense_maxsim_kernel<TN, QRES, TF32>;
+  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages);
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+  if (e != cudaSuccess) return TMS_ERR_CUDA;
+  const unsigned grid = static_cast<unsigned>(p.n_ranges) * static_cast<unsigned>(p.n_groups);
+  kern<<<grid, kThreads, L.total, st>>>(qm, dm, args);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_dense(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
+                 const DensePlan& p, bool tf32, cudaStream_t st) {
+  if (tf32) {
+    if (p.TN == 256)
+      return p.qres ? launch_dense_t<256, true, true>(qm, dm, args, p, st)
+                    : launch_dense_t<256, false, true>(qm, dm, args, p, st);
+    return p.qres ? launch_dense_t<128, true, true>(qm, dm, args, p, st)
+                  : launch_dense_t<128, false, true>(qm, dm, args, p, st);
+  }
+  if (p.TN == 256)
+    return p.qres ? launch_dense_t<256, true, false>(qm, dm, args, p, st)
+                  : launch_dense_t<256, false, false>(qm, dm, args, p, st);
+  return p.qres ? launch_dense_t<128, true, false>(qm, dm, args, p, st)
+                : launch_dense_t<128, false, false>(qm, dm, args, p, st);
+}
+
+}  // namespace
+
+}  // namespace tms
+
+using namespace tms;
+
+extern "C" size_t tms_dense_workspace_size(int dtype, int64_t n_queries, int64_t nq, int64_t d,
+                                           int64_t n_docs, int out_mode) {
+  if (n_queries <= 0 || nq <= 0 || d <= 0 || n_docs < 0) return 0;
+  DensePlan p;
+  if (plan_dense(dtype, n_queries, nq, d, n_docs, 1, out_mode, 148, 232448, &p) != TMS_OK)
+    return 0;
+  return p.qp_bytes + p.partial_bytes;
+}
+
+extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int64_t nq,
+                                int64_t d, const void* D, int64_t n_tokens,
+                                const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                                float* out, int out_mode, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (dtype != TMS_F16 && dtype != TMS_BF16 && dtype != TMS_F32) return TMS_ERR_INVALID;
+  if (out_mode != TMS_OUT_SCORE && out_mode != TMS_OUT_TOKEN_MAX) return TMS_ERR_INVALID;
+  if (n_queries < 0 || nq < 0 || d <= 0 || n_docs < 0 || n_tokens < 0) return TMS_ERR_INVALID;
+  if (n_queries == 0 || n_docs == 0) return TMS_OK;
+  if (nq == 0) return TMS_ERR_INVALID;
+  if (!Q || !out || (n_tokens > 0 && !D)) return TMS_ERR_INVALID;
+  if (!doc_offsets && nd_uniform < 0) return TMS_ERR_INVALID;
+  if (n_tokens >= (int64_t(1) << 31)) return TMS_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(Q) & 15) || (reinterpret_cast<uintptr_t>(D) & 15))
+    return TMS_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+
+  const int64_t out_elems = (out_mode == TMS_OUT_SCORE) ? n_queries * n_docs : n_queries * n_docs * nq;
+  if (n_tokens == 0 || (!doc_offsets && nd_uniform == 0)) {
+    // No token at all: every document is empty and scores -inf.
+    fill_kernel<<<dev->num_sms * 4, 256, 0, st>>>(out, out_elems, -__builtin_huge_valf());
+    return cuda_status(cudaGetLastError());
+  }
+  if (!doc_offsets && n_docs * nd_uniform > n_tokens) return TMS_ERR_INVALID;
+
+  DensePlan p;
+  int rc = plan_dense(dtype, n_queries, nq, d, n_docs, n_tokens, out_mode, dev->num_sms,
+                      dev->max_smem_optin, &p);
+  if (rc != TMS_OK) return rc;
+  if (!workspace || workspace_bytes < p.qp_bytes + p.partial_bytes) return TMS_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 1023) return TMS_ERR_INVALID;
+
+  uint8_t* qp = static_cast<uint8_t*>(workspace);
+  float* partial = reinterpret_cast<float*>(qp + p.qp_bytes);
+  const int row_bytes = static_cast<int>(d * p.esize);
+  const int vpr = row_bytes / 16;
+  const int64_t n_vec = static_cast<int64_t>(p.n_mtiles) * kQTileRows * vpr;
+  {
+    int blocks = static_cast<int>((n_vec + 255) / 256);
+    if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+    pack_query_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(Q),
+                                                    reinterpret_cast<uint4*>(qp), n_vec, vpr,
+                                                    static_cast<int>(nq), p.nchunk,
+                                                    p.n_chunks_total);
+    if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
+  }
+
+  const CUtensorMapDataType dt = (dtype == TMS_F16)    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : (dtype == TMS_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap qm, dm;
+  rc = encode_tmap_2d(&qm, dt, qp, static_cast<uint64_t>(d),
+                      static_cast<uint64_t>(p.n_mtiles) * kQTileRows, row_bytes, p.cw, kQTileRows);
+  if (rc != TMS_OK) return rc;
+  rc = encode_tmap_2d(&dm, dt, D, static_cast<uint64_t>(d), static_cast<uint64_t>(n_tokens),
+                      row_bytes, p.cw, p.TN);
+  if (rc != TMS_OK) return rc;
+
+  DenseArgs args;
+  args.docs.offsets = doc_offsets;
+  args.docs.n_docs = n_docs;
+  args.docs.nd = doc_offsets ? 0 : nd_uniform;
+  args.out = (out_mode == TMS_OUT_SCORE && p.nchunk > 1) ? partial : out;
+  args.err = dev->err_word;
+  args.timeout_ns = wait_timeout_ns();
+  args.n_chunks_total = p.n_chunks_total;
+  args.nchunk = p.nchunk;
+  args.nq = static_cast<int>(nq);
+  args.n_mtiles = p.n_mtiles;
+  args.G = p.G;
+  args.n_groups = p.n_groups;
+  args.n_ranges = p.n_ranges;
+  args.kc = p.kc;
+  args.stages = p.stages;
+  args.out_mode = out_mode;
+  args.ab_format = (dtype == TMS_F16) ? 0u : (dtype == TMS_BF16) ? 1u : 2u;
+  args.debug_flags = debug_flags();
+
+  rc = launch_dense(qm, dm, args, p, dtype == TMS_F32, st);
+  if (rc != TMS_OK) return rc;
+  if (out_mode == TMS_OUT_SCORE && p.nchunk > 1) {
+    const int64_t total = n_queries * n_docs;
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+    sum_query_chunks_kernel<<<blocks, 256, 0, st>>>(partial, out, n_queries, n_docs, p.nchunk);
+    return cuda_status(cudaGetLastError());
+  }
+  return TMS_OK;
+}
+
+// Exposes the launch plan for tests and the benchmark (not part of the stable ABI).
+extern "C" int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int64_t d,
+                                   int64_t n_docs, int64_t n_tokens, int out_mode, int num_sms,
+                                   int64_t* info /* 10 entries */) {
+  DensePlan p;
+  int rc = plan_dense(dtype, n_queries, nq, d, n_docs, n_tokens, out_mode, num_sms, 232448, &p);
+  if (rc != TMS_OK) return rc;
+  info[0] = p.TN;
+  info[1] = p.qres;
+  info[2] = p.G;
+  info[3] = p.stages;
+  info[4] = p.n_groups;
+  info[5] = p.n_ranges;
+  info[6] = p.n_mtiles;
+  info[7] = p.kc;
+  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages).total;
+  info[9] = static_cast<int64_t>(p.n_ranges) * p.n_groups;
+  return TMS_OK;
+}

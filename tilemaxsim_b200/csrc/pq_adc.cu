@@ -1,0 +1,279 @@
+// pq_adc.cu -- MaxSim straight from product-quantization codes (asymmetric distance computation).
+//
+//   table[q, i, m, k] = <Q[q, i, m*dsub:(m+1)*dsub], C[m, k, :]>           (fp32)
+//   score[q, doc]    = sum_i max_{j in doc} sum_m table[q, i, m, codes[j, m]]
+//
+// Reference: src/flash_pqsim_kernel.py:31-67 (_build_distance_table_kernel), :127-173
+// (_flash_pqsim_batched_score_kernel: per (query token, doc) running max of the m-ordered table
+// sums) and :213-280 (score_batch sums the per-token maxima; score_single for one document).
+//
+// B200 design: one CTA owns a slice of QS query tokens of one query and a range of documents. It
+// builds that slice's table in shared memory as T[m][k][QS] (fp32, so one code byte fetches the
+// entries of all QS query tokens with 128-bit shared loads), then a warp scores one document at a
+// time: lanes stride over the document's tokens, read each token's M code bytes with 16-byte
+// vector loads, accumulate the M table entries per query token in m order (the reference's
+// summation order), keep per-lane running maxima, and reduce them across the warp when the
+// document ends. Codes are never decoded to vectors and the table never touches HBM.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "tms_device.cuh"
+#include "tms_internal.h"
+
+namespace tms {
+namespace {
+
+constexpr int kPqThreads = 512;
+constexpr int kPqTableBudget = 200 * 1024;
+constexpr float kNegInfPq = -__builtin_huge_valf();
+
+__device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) {
+  if (dtype == TMS_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  if (dtype == TMS_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+// table[((q*nq + i) * M + m) * K + k] in fp32, one thread per entry (the reference's layout).
+__global__ void pq_table_kernel(const void* __restrict__ Q, int q_dtype, int64_t n_rows,
+                                const void* __restrict__ cb, int cb_dtype, int M, int K, int dsub,
+                                float* __restrict__ table) {
+  const int64_t total = n_rows * M * K;
+  const int d = M * dsub;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / (static_cast<int64_t>(M) * K);
+    const int rem = static_cast<int>(e - r * M * K);
+    const int m = rem / K, k = rem - m * K;
+    float acc = 0.0f;
+    for (int t = 0; t < dsub; ++t)
+      acc = fmaf(load_elem(Q, q_dtype, r * d + m * dsub + t),
+                 load_elem(cb, cb_dtype, (static_cast<int64_t>(m) * K + k) * dsub + t), acc);
+    table[e] = acc;
+  }
+}
+
+struct PqArgs {
+  const void* Q;
+  const void* cb;
+  const uint8_t* codes;
+  DocLayout docs;
+  float* out;  // (n_queries * nslice, n_docs): slice partial scores (final scores if nslice == 1)
+  int q_dtype, cb_dtype;
+  int nq, M, K, dsub;
+  int nslice;      // query-token slices per query
+  int n_doc_parts;
+};
+
+template <int QS, bool M16>
+__global__ void __launch_bounds__(kPqThreads)
+    pq_maxsim_kernel(const PqArgs a) {
+  extern __shared__ __align__(16) float tbl[];  // [M][K][QS]
+  const int slice_id = blockIdx.x / a.n_doc_parts;
+  const int part = blockIdx.x - slice_id * a.n_doc_parts;
+  const int q = slice_id / a.nslice;
+  const int i0 = (slice_id - q * a.nslice) * QS;
+  const int d = a.M * a.dsub;
+
+  // Build T[m][k][s] = <Q[q, i0+s, m-slice], C[m, k]> (zero for query tokens past nq).
+  const int n_ent = a.M * a.K * QS;
+  for (int e = threadIdx.x; e < n_ent; e += blockDim.x) {
+    const int s = e % QS;
+    const int mk = e / QS;
+    const int m = mk / a.K, k = mk - m * a.K;
+    const int i = i0 + s;
+    float acc = 0.0f;
+    if (i < a.nq) {
+      const int64_t qrow = (static_cast<int64_t>(q) * a.nq + i) * d + m * a.dsub;
+      const int64_t crow = (static_cast<int64_t>(m) * a.K + k) * a.dsub;
+      for (int t = 0; t < a.dsub; ++t)
+        acc = fmaf(load_elem(a.Q, a.q_dtype, qrow + t), load_elem(a.cb, a.cb_dtype, crow + t), acc);
+    }
+    tbl[e] = acc;
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_warps = blockDim.x >> 5;
+  const int64_t n_docs = a.docs.n_docs;
+  const int64_t doc_begin = n_docs * part / a.n_doc_parts;
+  const int64_t doc_end = n_docs * (part + 1) / a.n_doc_parts;
+  const int ns = min(QS, a.nq - i0);
+  const uint32_t kmax = static_cast<uint32_t>(a.K - 1);
+  for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
+    const int64_t t_lo = a.docs.start(doc), t_hi = a.docs.start(doc + 1);
+    float run[QS];
+#pragma unroll
+    for (int s = 0; s < QS; ++s) run[s] = kNegInfPq;
+    for (int64_t j = t_lo + lane; j < t_hi; j += 32) {
+      float acc[QS];
+#pragma unroll
+      for (int s = 0; s < QS; ++s) acc[s] = 0.0f;
+      const uint8_t* row = a.codes + j * a.M;
+      if (M16) {
+        const uint4 c4 = __ldg(reinterpret_cast<const uint4*>(row));
+        const uint32_t w[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          uint32_t code = (w[m >> 2] >> (8 * (m & 3))) & 0xffu;
+          if (kmax < 255u) code = min(code, kmax);  // a code >= K never reads past the table
+          const float* e = tbl + (m * a.K + code) * QS;
+          if (QS % 4 == 0) {
+#pragma unroll
+            for (int s = 0; s < QS; s += 4) {
+              const float4 t = *reinterpret_cast<const float4*>(e + s);
+              acc[s] += t.x;
+              acc[s + 1] += t.y;
+              acc[s + 2] += t.z;
+              acc[s + 3] += t.w;
+            }
+          } else {
+#pragma unroll
+            for (int s = 0; s < QS; ++s) acc[s] += e[s];
+          }
+        }
+      } else {
+        for (int m = 0; m < a.M; ++m) {
+          const uint32_t code = min(static_cast<uint32_t>(__ldg(row + m)), kmax);
+          const float* e = tbl + (m * a.K + code) * QS;
+#pragma unroll
+          for (int s = 0; s < QS; ++s) acc[s] += e[s];
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < QS; ++s) run[s] = fmaxf(run[s], acc[s]);
+    }
+    float total = 0.0f;
+#pragma unroll
+    for (int s = 0; s < QS; ++s) {
+      const float mx = warp_max(run[s]);
+      if (s < ns) total += mx;
+    }
+    if (lane == 0) a.out[static_cast<int64_t>(slice_id) * n_docs + doc] = total;
+  }
+}
+
+__global__ void pq_sum_slices_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                     int64_t n_queries, int64_t n_docs, int nslice) {
+  const int64_t total = n_queries * n_docs;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t q = i / n_docs, dd = i - q * n_docs;
+    float s = 0.0f;
+    for (int p = 0; p < nslice; ++p) s += partial[(q * nslice + p) * n_docs + dd];
+    out[i] = s;
+  }
+}
+
+int pick_qs(int64_t M, int64_t K, int64_t nq) {
+  int qs = 8;
+  while (qs > 1 && M * K * qs * 4 > kPqTableBudget) qs >>= 1;
+  while (qs > 1 && qs / 2 >= nq) qs >>= 1;  // no wider than the query
+  return qs;
+}
+
+template <int QS>
+int launch_pq_t(const PqArgs& a, bool m16, unsigned grid, size_t smem, cudaStream_t st) {
+  auto k = m16 ? pq_maxsim_kernel<QS, true> : pq_maxsim_kernel<QS, false>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return TMS_ERR_CUDA;
+  k<<<grid, kPqThreads, smem, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace tms
+
+using namespace tms;
+
+extern "C" int tms_pq_table(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
+                            const void* codebook, int cb_dtype, int64_t M, int64_t K, int64_t dsub,
+                            float* table, void* stream) {
+  if (n_queries < 0 || nq < 0 || M <= 0 || K <= 0 || dsub <= 0) return TMS_ERR_INVALID;
+  if (q_dtype < TMS_F16 || q_dtype > TMS_F32 || cb_dtype < TMS_F16 || cb_dtype > TMS_F32)
+    return TMS_ERR_INVALID;
+  if (n_queries * nq == 0) return TMS_OK;
+  if (!Q || !codebook || !table) return TMS_ERR_INVALID;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  const int64_t total = n_queries * nq * M * K;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > dev->num_sms * 16) blocks = dev->num_sms * 16;
+  pq_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      Q, q_dtype, n_queries * nq, codebook, cb_dtype, static_cast<int>(M), static_cast<int>(K),
+      static_cast<int>(dsub), table);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K,
+                                        int64_t n_docs) {
+  if (n_queries <= 0 || nq <= 0 || M <= 0 || K <= 0 || n_docs < 0) return 0;
+  const int qs = pick_qs(M, K, nq);
+  const int64_t nslice = (nq + qs - 1) / qs;
+  return nslice > 1 ? static_cast<size_t>(n_queries * nslice * n_docs) * 4 : 0;
+}
+
+extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
+                             const void* codebook, int cb_dtype, int64_t M, int64_t K,
+                             int64_t dsub, const uint8_t* codes, int64_t n_tokens,
+                             const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                             float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_queries < 0 || nq <= 0 || M <= 0 || K <= 0 || dsub <= 0 || n_docs < 0 || n_tokens < 0)
+    return TMS_ERR_INVALID;
+  if (q_dtype < TMS_F16 || q_dtype > TMS_F32 || cb_dtype < TMS_F16 || cb_dtype > TMS_F32)
+    return TMS_ERR_INVALID;
+  if (n_queries == 0 || n_docs == 0) return TMS_OK;
+  if (K > 256 || M > 4096) return TMS_ERR_UNSUPPORTED;  // codes are bytes
+  if (!Q || !codebook || !out || (n_tokens > 0 && !codes)) return TMS_ERR_INVALID;
+  if (!doc_offsets && (nd_uniform < 0 || n_docs * nd_uniform > n_tokens)) return TMS_ERR_INVALID;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  const int qs = pick_qs(M, K, nq);
+  const size_t smem = static_cast<size_t>(M * K * qs) * 4;
+  if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
+  const int nslice = static_cast<int>((nq + qs - 1) / qs);
+  const size_t need = tms_pq_workspace_size(n_queries, nq, M, K, n_docs);
+  if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
+  const bool m16 = (M == 16) && ((reinterpret_cast<uintptr_t>(codes) & 15) == 0);
+
+  PqArgs a;
+  a.Q = Q;
+  a.cb = codebook;
+  a.codes = codes;
+  a.docs.offsets = doc_offsets;
+  a.docs.n_docs = n_docs;
+  a.docs.nd = doc_offsets ? 0 : nd_uniform;
+  a.out = nslice > 1 ? static_cast<float*>(workspace) : out;
+  a.q_dtype = q_dtype;
+  a.cb_dtype = cb_dtype;
+  a.nq = static_cast<int>(nq);
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.dsub = static_cast<int>(dsub);
+  a.nslice = nslice;
+  const int64_t slices = n_queries * nslice;
+  int64_t parts = (2LL * dev->num_sms + slices - 1) / slices;
+  const int64_t max_parts = (n_docs + 15) / 16;  // at least ~16 docs per CTA
+  if (parts > max_parts) parts = max_parts;
+  if (parts < 1) parts = 1;
+  if (slices * parts > 0x7fffffffLL) return TMS_ERR_UNSUPPORTED;
+  a.n_doc_parts = static_cast<int>(parts);
+  const unsigned grid = static_cast<unsigned>(slices * parts);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  switch (qs) {
+    case 8: rc = launch_pq_t<8>(a, m16, grid, smem, st); break;
+    case 4: rc = launch_pq_t<4>(a, m16, grid, smem, st); break;
+    case 2: rc = launch_pq_t<2>(a, m16, grid, smem, st); break;
+    default: rc = launch_pq_t<1>(a, m16, grid, smem, st); break;
+  }
+  if (rc != TMS_OK || nslice == 1) return rc;
+  const int64_t total = n_queries * n_docs;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  pq_sum_slices_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(workspace), out,
+                                               n_queries, n_docs, nslice);
+  return cuda_status(cudaGetLastError());
+}

@@ -1,0 +1,41 @@
+// tms_internal.h -- host-side helpers shared by the library's translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/tilemaxsim.h"
+
+namespace tms {
+
+// Per-device facts and the address of the device error word (set up once per device).
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  uint32_t* err_word = nullptr;
+};
+// Returns nullptr (and sets *status) when the current device cannot be queried.
+const DeviceInfo* current_device_info(int* status);
+
+// Wait limit for the bounded mbarrier waits, in nanoseconds (default 2 s; tms_set_debug changes it).
+uint64_t wait_timeout_ns();
+// Test hook flags (tms_set_debug); 0 in normal operation.
+int debug_flags();
+
+// Encodes a 2-D row-major tensor map: `rows` rows of `inner` elements, row stride in bytes, box of
+// box_inner x box_rows elements, 128-byte swizzle, zero fill outside the tensor.
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                   uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_rows);
+
+// Integer environment override (tuning and benchmarking only); `fallback` when unset.
+long env_int(const char* name, long fallback);
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TMS_OK : TMS_ERR_CUDA; }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace tms

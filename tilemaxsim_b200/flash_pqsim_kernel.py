@@ -1,0 +1,117 @@
+"""Drop-in replacement for the reference's ``src/flash_pqsim_kernel.py`` (PQ / ADC MaxSim).
+
+``TileMaxSimPQ(codebook)`` keeps the reference's attributes (``codebook, M, K, dsub, d``) and
+methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_pqsim_kernel.py:
+176-280). Scoring runs in the sm_100a ADC kernel (C ABI ``tms_pq_maxsim``): each CTA builds its
+query slice's distance table in shared memory and scores straight from the uint8 codes, so neither
+the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote both).
+``score_queries`` is the additive multi-query, ragged-corpus entry point.
+``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _codes_u8(codes: torch.Tensor) -> torch.Tensor:
+    if codes.dtype != torch.uint8:
+        codes = codes.to(torch.uint8)  # the reference also accepts int32 codes (< 256)
+    return codes if codes.is_contiguous() else codes.contiguous()
+
+
+class TileMaxSimPQ:
+    """MaxSim over product-quantized documents (reference: src/flash_pqsim_kernel.py:176-280)."""
+
+    def __init__(self, codebook: torch.Tensor):
+        """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256."""
+        self.codebook = codebook.contiguous()
+        self.M, self.K, self.dsub = codebook.shape
+        self.d = self.M * self.dsub
+        if self.codebook.dtype not in _lib.DTYPE_CODE:
+            raise TypeError(f"codebook dtype {codebook.dtype} not supported")
+
+    def _q(self, Q: torch.Tensor) -> torch.Tensor:
+        if Q.dtype not in _lib.DTYPE_CODE:
+            Q = Q.float()
+        return Q if Q.is_contiguous() else Q.contiguous()
+
+    def build_distance_table(self, Q: torch.Tensor) -> torch.Tensor:
+        """(Nq, d) queries -> (Nq, M, K) fp32 table, T[q,m,k] = <Q[q, m-slice], C[m,k]>
+        (reference: src/flash_pqsim_kernel.py:190-211)."""
+        Nq = Q.shape[0]
+        assert Q.shape[1] == self.d
+        lib = _lib.load()
+        dev = _lib.require_cuda(Q, self.codebook)
+        Q = self._q(Q)
+        with torch.cuda.device(dev):
+            table = torch.empty(Nq, self.M, self.K, dtype=torch.float32, device=dev)
+            rc = lib.tms_pq_table(ctypes.c_void_p(Q.data_ptr()), _lib.DTYPE_CODE[Q.dtype], 1, Nq,
+                                  ctypes.c_void_p(self.codebook.data_ptr()), _lib.DTYPE_CODE[self.codebook.dtype],
+                                  self.M, self.K, self.dsub, ctypes.c_void_p(table.data_ptr()),
+                                  ctypes.c_void_p(_lib.stream_handle(dev)))
+            _lib.check(rc, "tms_pq_table")
+        return table
+
+    def _score(self, Qb: torch.Tensor, codes_tokens: torch.Tensor, offsets: torch.Tensor | None,
+               n_docs: int, nd: int) -> torch.Tensor:
+        lib = _lib.load()
+        tensors = [Qb, codes_tokens, self.codebook] + ([offsets] if offsets is not None else [])
+        dev = _lib.require_cuda(*tensors)
+        Bq, Nq, d = Qb.shape
+        if d != self.d:
+            raise ValueError(f"queries have d={d}, codebook expects d={self.d}")
+        if codes_tokens.shape[-1] != self.M:
+            raise ValueError(f"codes have {codes_tokens.shape[-1]} sub-quantizers, codebook has {self.M}")
+        Qb = self._q(Qb)
+        codes_tokens = _codes_u8(codes_tokens)
+        with torch.cuda.device(dev):
+            out = torch.empty(Bq, n_docs, dtype=torch.float32, device=dev)
+            if Bq == 0 or n_docs == 0:
+                return out
+            ws_bytes = lib.tms_pq_workspace_size(Bq, Nq, self.M, self.K, n_docs)
+            ws, ws_ptr = _lib.workspace(ws_bytes, dev, align=256)
+            rc = lib.tms_pq_maxsim(
+                ctypes.c_void_p(Qb.data_ptr()), _lib.DTYPE_CODE[Qb.dtype], Bq, Nq,
+                ctypes.c_void_p(self.codebook.data_ptr()), _lib.DTYPE_CODE[self.codebook.dtype],
+                self.M, self.K, self.dsub, ctypes.c_void_p(codes_tokens.data_ptr()), codes_tokens.shape[0],
+                ctypes.c_void_p(offsets.data_ptr() if offsets is not None else 0), n_docs, nd,
+                ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws_ptr), ws_bytes,
+                ctypes.c_void_p(_lib.stream_handle(dev)))
+            _lib.check(rc, "tms_pq_maxsim")
+            del ws
+        return out
+
+    def score_batch(self, Q: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
+        """(Nq, d) query vs (B, Nd, M) codes -> (B,) fp32 (reference: src/flash_pqsim_kernel.py:213-252)."""
+        B, Nd, M = codes.shape
+        assert M == self.M
+        return self._score(Q.unsqueeze(0), codes.reshape(B * Nd, M), None, B, Nd)[0]
+
+    def score_single(self, Q: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
+        """(Nq, d) query vs one document's (Nd, M) codes -> 0-d fp32 (reference: :254-280)."""
+        Nd, M = codes.shape
+        assert M == self.M
+        return self._score(Q.unsqueeze(0), codes, None, 1, Nd)[0, 0]
+
+    def score_queries(self, Qb: torch.Tensor, codes_tokens: torch.Tensor, doc_offsets: torch.Tensor) -> torch.Tensor:
+        """B_q queries (B_q, Nq, d) vs a ragged corpus of codes (T, M) with int64 offsets (n+1,)
+        -> (B_q, n) fp32; an empty document scores -inf."""
+        if doc_offsets.dtype != torch.int64:
+            doc_offsets = doc_offsets.to(torch.int64)
+        return self._score(Qb, codes_tokens, doc_offsets.contiguous(), doc_offsets.numel() - 1, 0)
+
+
+def pytorch_pqsim_baseline(Q: torch.Tensor, codebook: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
+    """Decompress-then-score PyTorch baseline (reference: src/flash_pqsim_kernel.py:283-313)."""
+    M, K, dsub = codebook.shape
+    B, Nd, _ = codes.shape
+    d = Q.shape[1]
+    D_approx = torch.zeros(B, Nd, d, dtype=torch.float32, device=Q.device)
+    for m in range(M):
+        D_approx[:, :, m * dsub:(m + 1) * dsub] = codebook[m][codes[:, :, m].long()].float()
+    S = torch.einsum("qd,bnd->bqn", Q.float(), D_approx)
+    return S.max(dim=-1).values.sum(dim=-1)
