@@ -40,6 +40,9 @@ CONFIGS = {
     "c3_256": (16, 32, 256, 50_000, 256, 256, 1000),
     "c3_768": (16, 32, 768, 50_000, 256, 256, 1000),
     "c5": (256, 32, 128, 1_250_000, 96, 160, 100),  # one eighth of the 10M-doc sharded corpus
+    # single query, the reference's best-case V2-MQ shape (Nd = 256, B = 100k): HBM-bound
+    "q1_nd256": (1, 32, 128, 100_000, 256, 256, 10),
+    "q1_ragged": (1, 32, 128, 400_000, 64, 300, 10),
 }
 
 

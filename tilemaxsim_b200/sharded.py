@@ -45,12 +45,12 @@ def merge_topk(vals: torch.Tensor, ids: torch.Tensor, k: int, group=None,
         return vals, ids
     world = dist.get_world_size(group)
     rows = vals.shape[0]
-    gv = torch.empty((world, rows, k), dtype=vals.dtype, device=vals.device)
-    gi = torch.empty((world, rows, k), dtype=ids.dtype, device=ids.device)
-    dist.all_gather_into_tensor(gv, vals, group=group)
+    gv = torch.empty((world * rows, k), dtype=vals.dtype, device=vals.device)
+    gi = torch.empty((world * rows, k), dtype=ids.dtype, device=ids.device)
+    dist.all_gather_into_tensor(gv, vals, group=group)  # rank-major concatenation along dim 0
     dist.all_gather_into_tensor(gi, ids, group=group)
-    cand_v = gv.permute(1, 0, 2).reshape(rows, world * k)
-    cand_i = gi.permute(1, 0, 2).reshape(rows, world * k)
+    cand_v = gv.view(world, rows, k).permute(1, 0, 2).reshape(rows, world * k)
+    cand_i = gi.view(world, rows, k).permute(1, 0, 2).reshape(rows, world * k)
     fn = topk_fn or topk
     return fn(cand_v.contiguous(), k, ids=cand_i.contiguous())
 
