@@ -43,6 +43,9 @@ CONFIGS = {
     # single query, the reference's best-case V2-MQ shape (Nd = 256, B = 100k): HBM-bound
     "q1_nd256": (1, 32, 128, 100_000, 256, 256, 10),
     "q1_ragged": (1, 32, 128, 400_000, 64, 300, 10),
+    # reduced corpora for ncu --set full captures (still larger than L2, a few hundred MB)
+    "c2_small": (64, 32, 128, 10_000, 64, 300, 1000),
+    "q1_small": (1, 32, 128, 20_000, 256, 256, 10),
 }
 
 
@@ -57,7 +60,7 @@ def peaks() -> dict:
 
 # ------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML every 200 ms while running."""
+    """Samples SM clock and clock-event reasons through NVML every 20 ms while running."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
@@ -86,7 +89,7 @@ class ClockSampler:
                 self.reasons.update(v for k, v in self.REASONS.items() if r & k)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.02)
 
     def __enter__(self):
         if self._h is not None:

@@ -71,7 +71,10 @@ const DeviceInfo* current_device_info(int* status) {
 }
 
 uint64_t wait_timeout_ns() { return g_timeout_ns; }
-int debug_flags() { return g_debug_flags; }
+int debug_flags() {
+  static const int env_flags = static_cast<int>(env_int("TMS_DEBUG_FLAGS", 0));
+  return g_debug_flags | env_flags;
+}
 
 long env_int(const char* name, long fallback) {
   const char* v = std::getenv(name);

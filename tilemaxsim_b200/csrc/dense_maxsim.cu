@@ -38,7 +38,8 @@ namespace tms {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 2 control warps + 8 epilogue warps
+constexpr int kEpiWarps = 8;
 constexpr int kQTileRows = 128;
 constexpr uint32_t kQChunkBytes = kQTileRows * 128;  // one 128-row x 128-byte K chunk of Q
 constexpr float kNegInf = -__builtin_huge_valf();
@@ -59,15 +60,22 @@ struct DenseArgs {
   int stages;
   int out_mode;
   uint32_t ab_format;  // MMA operand format: 0 = f16, 1 = bf16, 2 = tf32
-  int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits)
+  int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits);
+                       // bits 2/3: skip the epilogue math / the MMAs (timing experiments only)
 };
 
-// Shared-memory carve-up, identical on host and device.
+// Shared-memory carve-up, identical on host and device. `split` (one query of <= 32 tokens) adds
+// the exchange area of the column-split epilogue and drops the per-row carries.
 struct SmemLayout {
-  uint32_t q_off, stage_off, stage_bytes, bar_off, carry_off, misc_off, total;
+  uint32_t q_off, stage_off, stage_bytes, bar_off, carry_off, x_off, misc_off, total;
+};
+struct PartMeta {  // one epilogue warp's summary of its column part (split mode)
+  int64_t head_doc;  // document whose end lies in the part (valid if has_b)
+  int64_t end_doc, end_dend;  // walk state after the part
+  int32_t has_b, pad;
 };
 __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G, int kc,
-                                                        int stages) {
+                                                        int stages, bool split) {
   SmemLayout L;
   L.q_off = 0;
   const uint32_t q_bytes = qres ? static_cast<uint32_t>(G * kc) * kQChunkBytes : 0u;
@@ -76,8 +84,11 @@ __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G
   L.bar_off = L.stage_off + static_cast<uint32_t>(stages) * L.stage_bytes;
   const uint32_t n_bars = 2u * stages + 6u;
   L.carry_off = (L.bar_off + n_bars * 8u + 15u) & ~15u;
-  L.misc_off = L.carry_off + static_cast<uint32_t>(G) * kQTileRows * 4u;
-  L.total = L.misc_off + 64u + 1024u;  // + slack to align the dynamic base to 1024
+  L.x_off = L.carry_off + (split ? 0u : static_cast<uint32_t>(G) * kQTileRows * 4u);
+  const uint32_t x_bytes =
+      split ? 2u * kEpiWarps * 32u * 4u + kEpiWarps * static_cast<uint32_t>(sizeof(PartMeta)) : 0u;
+  L.misc_off = (L.x_off + x_bytes + 15u) & ~15u;
+  L.total = L.misc_off + 64u;
   return L;
 }
 
@@ -85,36 +96,52 @@ struct RangeInfo {
   int64_t doc_lo, doc_hi, tok_lo, tok_hi;
 };
 
-// Max over v[lo, hi) (empty -> -inf).
-__device__ __forceinline__ float range_max(const float (&v)[32], int lo, int hi) {
-  if (lo == 0 && hi == 32) {
-    float m0 = fmaxf(v[0], v[1]), m1 = fmaxf(v[2], v[3]), m2 = fmaxf(v[4], v[5]),
-          m3 = fmaxf(v[6], v[7]);
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+
+// Three-input fp32 max (PTX max.f32 with three sources, sm_100a).
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+  return r;
+}
+
+// max(acc, r[0..31]) with four independent chains.
+__device__ __forceinline__ float max32(float acc, const uint32_t (&r)[32]) {
+  float m[4];
 #pragma unroll
-    for (int i = 8; i < 32; i += 8) {
-      m0 = fmaxf(m0, fmaxf(v[i + 0], v[i + 1]));
-      m1 = fmaxf(m1, fmaxf(v[i + 2], v[i + 3]));
-      m2 = fmaxf(m2, fmaxf(v[i + 4], v[i + 5]));
-      m3 = fmaxf(m3, fmaxf(v[i + 6], v[i + 7]));
-    }
-    return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-  }
-  float m = kNegInf;
+  for (int j = 0; j < 4; ++j) m[j] = fmax3(u2f(r[j]), u2f(r[j + 4]), u2f(r[j + 8]));
+#pragma unroll
+  for (int i = 12; i < 28; i += 8)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m[j] = fmax3(m[j], u2f(r[i + j]), u2f(r[i + 4 + j]));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) m[j] = fmaxf(m[j], u2f(r[28 + j]));
+  return fmax3(fmax3(acc, m[0], m[1]), m[2], m[3]);
+}
+
+// max(acc, r[lo..hi)) (acc when the range is empty).
+__device__ __forceinline__ float range_max32(float acc, const uint32_t (&r)[32], int lo, int hi) {
+  float m0 = acc, m1 = kNegInf;
   const uint32_t span = static_cast<uint32_t>(hi - lo);
 #pragma unroll
-  for (int i = 0; i < 32; ++i)
-    if (static_cast<uint32_t>(i - lo) < span) m = fmaxf(m, v[i]);
-  return m;
+  for (int i = 0; i < 32; i += 4) {
+    const float a0 = static_cast<uint32_t>(i - lo) < span ? u2f(r[i]) : kNegInf;
+    const float a1 = static_cast<uint32_t>(i + 1 - lo) < span ? u2f(r[i + 1]) : kNegInf;
+    const float a2 = static_cast<uint32_t>(i + 2 - lo) < span ? u2f(r[i + 2]) : kNegInf;
+    const float a3 = static_cast<uint32_t>(i + 3 - lo) < span ? u2f(r[i + 3]) : kNegInf;
+    m0 = fmax3(m0, a0, a1);
+    m1 = fmax3(m1, a2, a3);
+  }
+  return fmaxf(m0, m1);
 }
 
 template <int TN, bool QRES, bool TF32>
 __global__ void __launch_bounds__(kThreads, 1)
     dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const bool split = a.n_chunks_total == 1;  // one query: column-split epilogue
+  const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages, split);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t q_s = sbase + L.q_off;
   const uint32_t st_s = sbase + L.stage_off;
@@ -137,6 +164,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int group = blockIdx.x - range * a.n_groups;
   const int m_first = group * a.G;
   const int g_this = min(a.G, a.n_mtiles - m_first);
+  // rows mode: the two epilogue groups take alternate query tiles (m parity). Only with an even
+  // number of tiles per CTA: then group g always owns TMEM slot g and waits on every phase of it
+  // in order (with an odd count a group would skip phases and a parity wait could match a stale
+  // completion two phases back).
+  const bool two_groups = !split && g_this >= 2 && (g_this & 1) == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -145,11 +177,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), 4);
+      mbar_init(acce_bar(b), split ? kEpiWarps : 4);
     }
     mbar_init(qfull_bar, 1);
     mbar_init(done_bar, 1);
-    *abort_flag = 0;
+    *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
+    if (*abort_flag) atomicCAS(a.err, 0u, kDevErrTimeout | 15u);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -183,8 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t doc_lo = rinfo->doc_lo, doc_hi = rinfo->doc_hi;
   const int64_t tok_lo = rinfo->tok_lo, tok_hi = rinfo->tok_hi;
   const uint64_t tmo = a.timeout_ns;
+  const bool dead = *abort_flag != 0;
 
-  if (warp == 0) {
+  if (dead) {
+    // misaligned shared memory: no role runs (the error word says why)
+  } else if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && !(a.debug_flags & 1)) {
       const uint64_t pol_d = (a.n_groups > 1) ? policy_evict_normal() : policy_evict_first();
@@ -257,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
+              if (a.debug_flags & 8) break;
               const uint64_t ad = sw128_kmajor_desc(a_base + 32u * k);
               const uint64_t bd = sw128_kmajor_desc(b_base + 32u * k);
               if (TF32)
@@ -283,13 +320,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
+    const int ew = warp - 2;  // epilogue warp 0..7
+    const int eg = ew >> 2;   // epilogue group (rows mode)
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
     const int row = lg * 32 + lane;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(lg * 32) << 16);
-    for (int m = 0; m < g_this; ++m) carry[m * kQTileRows + row] = kNegInf;
     const DocLayout docs = a.docs;
+    // Document ends are fetched 32 at a time (one coalesced load per warp) and handed out with
+    // shuffles, so walking the document boundaries costs one global load per 32 documents.
+    int64_t e_base = INT64_MIN / 2;  // first document whose end is cached in `ends`
+    int64_t ends = 0;
     auto doc_end = [&](int64_t dd) -> int64_t {
-      return dd < doc_hi ? docs.start(dd + 1) : INT64_MAX;
+      if (dd >= doc_hi) return INT64_MAX;
+      int64_t idx = dd - e_base;
+      if (idx < 0 || idx >= 32) {
+        e_base = dd;
+        const int64_t j = dd + 1 + lane;
+        ends = (j <= docs.n_docs) ? docs.start(j) : INT64_MAX;
+        idx = 0;
+      }
+      return __shfl_sync(0xffffffffu, ends, static_cast<int>(idx));
     };
     auto emit = [&](int chunk, int64_t dd, float rm) {
       const int q = chunk / a.nchunk;
@@ -302,64 +352,198 @@ __global__ void __launch_bounds__(kThreads, 1)
         a.out[(static_cast<int64_t>(q) * docs.n_docs + dd) * a.nq + rq] = rm;
       }
     };
+    auto wait_full = [&](uint32_t slot, uint32_t uu) -> bool {
+      int w = 0;
+      if (lane == 0) w = mbar_wait(accf_bar(slot), (uu >> 1) & 1u, abort_flag, tmo, a.err, 8);
+      return __shfl_sync(0xffffffffu, w, 0) != 0;
+    };
+    const bool skip_math = (a.debug_flags & 4) != 0;
 
     int64_t doc = doc_lo;
     int64_t dend = doc_end(doc);
     uint32_t u = 0;
     bool ok = true;
-    for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
-      int64_t next_doc = doc, next_dend = dend;
-      for (int m = 0; m < g_this; ++m, ++u) {
+    if (split) {
+      // ---- split mode: one query replicated in all four lane quarters; warp ew owns columns
+      // [32*ew, 32*ew+32) of every tile. Documents wholly inside a part are emitted by its warp;
+      // the part's first (head) and last (tail) partial maxima go through shared memory and
+      // warp 0 of the epilogue chains them across parts and tiles.
+      float* xhead = reinterpret_cast<float*>(smem + L.x_off);
+      float* xtail = xhead + kEpiWarps * 32;
+      PartMeta* xmeta = reinterpret_cast<PartMeta*>(xtail + kEpiWarps * 32);
+      constexpr int kParts = TN / 32;
+      float running = kNegInf;  // combine warp: max of the document open at the last part's end
+      for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN, ++u) {
         const uint32_t slot = u & 1u;
-        int w = 0;
-        if (lane == 0) w = mbar_wait(accf_bar(slot), (u >> 1) & 1u, abort_flag, tmo, a.err, 8);
-        ok = __shfl_sync(0xffffffffu, w, 0) != 0;
-        if (!ok) break;
+        const bool w_ok = wait_full(slot, u);
         tc_fence_after();
-        const int chunk = (m_first + m) * 4 + lg;
-        if (chunk < a.n_chunks_total) {
-          float rm = carry[m * kQTileRows + row];
-          int64_t dd = doc, de = dend;
-#pragma unroll 1
-          for (int j = 0; j < TN / 32; ++j) {
-            const int64_t c0 = t0 + 32 * j;
-            if (c0 >= tok_hi) break;
-            float v[32];
-            tmem_ld32(t_lane + slot * TN + 32u * j, v);
-            const int n = (tok_hi - c0 < 32) ? static_cast<int>(tok_hi - c0) : 32;
+        const int ncol = (tok_hi - t0 < TN) ? static_cast<int>(tok_hi - t0) : TN;
+        const int pc0 = 32 * ew;
+        float head = kNegInf, tail = kNegInf;
+        int has_b = 0;
+        int64_t head_doc = -1, dd = doc, de = dend;
+        if (w_ok && ew < kParts && pc0 < ncol) {
+          uint32_t r[32];
+          tmem_ld32_async(t_lane + slot * TN + pc0, r);
+          tmem_wait_ld32(r);
+          if (!skip_math) {
+            auto rel = [&](int64_t e) -> int {
+              const int64_t x = e - t0;
+              return x > 4 * TN ? 4 * TN : static_cast<int>(x);
+            };
+            int dcol = rel(de);
+            while (dcol < pc0) {  // documents that end before this part belong to earlier parts
+              ++dd;
+              de = doc_end(dd);
+              dcol = rel(de);
+            }
+            const int n = (ncol - pc0 < 32) ? ncol - pc0 : 32;
+            float rm = kNegInf;
             int lo = 0;
             while (true) {
-              const int hi = (de - c0 < n) ? static_cast<int>(de - c0) : n;
-              rm = fmaxf(rm, range_max(v, lo, hi));
-              if (de - c0 >= n) break;
-              emit(chunk, dd, rm);
+              const int hi = (dcol - pc0 < n) ? dcol - pc0 : n;
+              rm = (lo == 0 && hi == 32) ? max32(rm, r) : range_max32(rm, r, lo, hi);
+              if (dcol - pc0 >= n) break;
+              if (!has_b) {
+                head = rm;
+                head_doc = dd;
+                has_b = 1;
+              } else {
+                emit(0, dd, rm);
+              }
               rm = kNegInf;
               ++dd;
               de = doc_end(dd);
+              dcol = rel(de);
               lo = hi;
             }
+            if (has_b) tail = rm; else head = rm;
           }
-          carry[m * kQTileRows + row] = rm;
-          next_doc = dd;
-          next_dend = de;
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acce_bar(slot));
+        if (lane == 0) mbar_arrive(acce_bar(slot));  // this warp is done with the TMEM slot
+        xhead[ew * 32 + lane] = head;
+        xtail[ew * 32 + lane] = tail;
+        if (lane == 0) {
+          xmeta[ew].head_doc = head_doc;
+          xmeta[ew].has_b = has_b;
+          xmeta[ew].end_doc = dd;
+          xmeta[ew].end_dend = de;
+        }
+        // all eight warps agree on whether every wait succeeded before anyone waits again
+        uint32_t all_ok;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.and.pred q, 1, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}\n"
+            : "=r"(all_ok)
+            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32)
+            : "memory");
+        if (!(ok = all_ok != 0)) break;
+        const int n_parts = (ncol + 31) / 32;
+        if (!skip_math) {
+          if (ew == 0) {
+            for (int pp = 0; pp < n_parts; ++pp) {
+              running = fmaxf(running, xhead[pp * 32 + lane]);
+              if (xmeta[pp].has_b) {
+                emit(0, xmeta[pp].head_doc, running);
+                running = xtail[pp * 32 + lane];
+              }
+            }
+          }
+          doc = xmeta[n_parts - 1].end_doc;
+          dend = xmeta[n_parts - 1].end_dend;
+        }
+        // the exchange area is reused by the next tile only after the combine has read it
+        if (ew == 0)
+          asm volatile("bar.arrive 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
+        else
+          asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
       }
-      doc = next_doc;
-      dend = next_dend;
-    }
-    if (ok) {
-      // Documents still open at the end of the range: the last one (ends at tok_hi) and any empty
-      // documents after it.
-      for (int m = 0; m < g_this; ++m) {
-        const int chunk = (m_first + m) * 4 + lg;
-        if (chunk >= a.n_chunks_total) continue;
-        float rm = carry[m * kQTileRows + row];
+      if (ok && ew == 0 && !skip_math) {
         for (int64_t dd = doc; dd < doc_hi; ++dd) {
-          emit(chunk, dd, rm);
-          rm = kNegInf;
+          emit(0, dd, running);
+          running = kNegInf;
+        }
+      }
+    } else if (eg == 0 || two_groups) {
+      // ---- rows mode: warp = one 32-row query chunk, all columns of the tile.
+      for (int m = 0; m < g_this; ++m)
+        if (!two_groups || (m & 1) == eg) carry[m * kQTileRows + row] = kNegInf;
+      for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+        int64_t next_doc = doc, next_dend = dend;
+        for (int m = 0; m < g_this; ++m, ++u) {
+          if (two_groups && (m & 1) != eg) continue;
+          const uint32_t slot = u & 1u;
+          if (!(ok = wait_full(slot, u))) break;
+          tc_fence_after();
+          const int chunk = (m_first + m) * 4 + lg;
+          if (chunk < a.n_chunks_total && !skip_math) {
+            float rm = carry[m * kQTileRows + row];
+            int64_t dd = doc, de = dend;
+            // Columns of this tile: [0, ncol) are tokens of the range; the open document ends
+            // at column dcol (>= 0, clamped far past the tile when it ends later).
+            const int ncol = (tok_hi - t0 < TN) ? static_cast<int>(tok_hi - t0) : TN;
+            auto rel = [&](int64_t e) -> int {
+              const int64_t x = e - t0;
+              return x > 4 * TN ? 4 * TN : static_cast<int>(x);
+            };
+            int dcol = rel(de);
+            const uint32_t tbase = t_lane + slot * TN;
+            uint32_t ra[32], rb[32];
+            tmem_ld32_async(tbase, ra);
+#pragma unroll
+            for (int b = 0; b < TN / 32; ++b) {
+              uint32_t(&cur)[32] = (b & 1) ? rb : ra;
+              uint32_t(&nxt)[32] = (b & 1) ? ra : rb;
+              const int cb = 32 * b;
+              if (cb < ncol) {
+                tmem_wait_ld32(cur);
+                if (b + 1 < TN / 32 && cb + 32 < ncol) tmem_ld32_async(tbase + cb + 32, nxt);
+                if (dcol >= cb + 32 && ncol >= cb + 32) {
+                  rm = max32(rm, cur);  // the whole block lies in the open document
+                } else {
+                  const int n = (ncol - cb < 32) ? ncol - cb : 32;
+                  int lo = 0;
+                  while (true) {
+                    const int hi = (dcol - cb < n) ? dcol - cb : n;
+                    rm = range_max32(rm, cur, lo, hi);
+                    if (dcol - cb >= n) break;
+                    emit(chunk, dd, rm);
+                    rm = kNegInf;
+                    ++dd;
+                    de = doc_end(dd);
+                    dcol = rel(de);
+                    lo = hi;
+                  }
+                }
+              }
+            }
+            carry[m * kQTileRows + row] = rm;
+            next_doc = dd;
+            next_dend = de;
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acce_bar(slot));
+        }
+        doc = next_doc;
+        dend = next_dend;
+      }
+      if (ok && !skip_math) {
+        // Documents still open at the end of the range: the last one (ends at tok_hi) and any
+        // empty documents after it.
+        for (int m = 0; m < g_this; ++m) {
+          if (two_groups && (m & 1) != eg) continue;
+          const int chunk = (m_first + m) * 4 + lg;
+          if (chunk >= a.n_chunks_total) continue;
+          float rm = carry[m * kQTileRows + row];
+          for (int64_t dd = doc; dd < doc_hi; ++dd) {
+            emit(chunk, dd, rm);
+            rm = kNegInf;
+          }
         }
       }
     }
@@ -374,15 +558,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Packs Q (n_queries, nq, d) into 128-row M tiles: chunk c (32 rows) = rows [32p, 32p+32) of query
-// c / nchunk (p = c % nchunk); rows past nq and chunks past the last query are zero.
+// c / nchunk (p = c % nchunk); rows past nq and chunks past the last query are zero. With
+// `replicate` (a single chunk) the chunk fills all four 32-row quarters of the tile.
 __global__ void pack_query_tiles_kernel(const uint4* __restrict__ q, uint4* __restrict__ qp,
                                         int64_t n_vec_total, int vec_per_row, int nq, int nchunk,
-                                        int n_chunks_total) {
+                                        int n_chunks_total, int replicate) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_vec_total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / vec_per_row;
     const int v = static_cast<int>(i - r * vec_per_row);
-    const int64_t c = r >> 5;
+    const int64_t c = replicate ? 0 : (r >> 5);  // replicate: the single chunk in all 4 quarters
     const int ln = static_cast<int>(r & 31);
     uint4 val = make_uint4(0, 0, 0, 0);
     if (c < n_chunks_total) {
@@ -439,7 +624,7 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
                          ? align_up(static_cast<size_t>(chunks) * n_docs * 4, 256)
                          : 0;
 
-  const int budget = max_smem - 2048 - 1024 - 64;
+  const int budget = max_smem - 2560 - 64;  // barriers, carries / exchange area, misc
   p->TN = static_cast<int>(env_int("TMS_DENSE_TN", p->kc <= 2 ? 256 : 128));
   if (p->TN != 128 && p->TN != 256) p->TN = 256;
   const int stage_d = p->kc * p->TN * 128;
@@ -450,12 +635,13 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     int gmax = (budget - 2 * stage_d) / qtile;
     gmax = static_cast<int>(env_int("TMS_DENSE_G", gmax < 4 ? gmax : 4));
     if (gmax < 1) gmax = 1;
-    // Per-CTA time grows with G x ceil(n_mtiles / G) (units per tile x token share): take the
-    // group size that minimises it, the larger one on ties (fewer re-reads of each doc tile).
+    // Per-CTA time grows with G x ceil(n_mtiles / G) (units per tile x token share), and an odd
+    // G (> 0) runs the epilogue on one warp group instead of two: take the group size that
+    // minimises the cost, the larger one on ties (fewer re-reads of each doc tile).
     int g = 1;
-    int64_t best = p->n_mtiles;
+    int64_t best = 2 * static_cast<int64_t>(p->n_mtiles);
     for (int c = 2; c <= gmax && c <= p->n_mtiles; ++c) {
-      const int64_t cost = static_cast<int64_t>(c) * ((p->n_mtiles + c - 1) / c);
+      const int64_t cost = static_cast<int64_t>(c) * ((p->n_mtiles + c - 1) / c) * ((c & 1) ? 2 : 1);
       if (cost <= best) { best = cost; g = c; }
     }
     p->n_groups = (p->n_mtiles + g - 1) / g;
@@ -474,7 +660,8 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
   }
   if (p->stages < 1) p->stages = 1;
-  const SmemLayout L = dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages);
+  const SmemLayout L =
+      dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages, p->n_chunks_total == 1);
   if (static_cast<int>(L.total) > max_smem) return TMS_ERR_UNSUPPORTED;
   int64_t ranges = p->n_groups >= num_sms ? 1 : num_sms / p->n_groups;
   ranges = env_int("TMS_DENSE_RANGES", ranges);
@@ -491,7 +678,7 @@ template <int TN, bool QRES, bool TF32>
 int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
                    const DensePlan& p, cudaStream_t st) {
   auto kern = dense_maxsim_kernel<TN, QRES, TF32>;
-  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages);
+  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_chunks_total == 1);
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (e != cudaSuccess) return TMS_ERR_CUDA;
@@ -577,7 +764,7 @@ extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int
     pack_query_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(Q),
                                                     reinterpret_cast<uint4*>(qp), n_vec, vpr,
                                                     static_cast<int>(nq), p.nchunk,
-                                                    p.n_chunks_total);
+                                                    p.n_chunks_total, p.n_chunks_total == 1);
     if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
   }
 
@@ -639,7 +826,7 @@ extern "C" int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int
   info[5] = p.n_ranges;
   info[6] = p.n_mtiles;
   info[7] = p.kc;
-  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages).total;
+  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_chunks_total == 1).total;
   info[9] = static_cast<int64_t>(p.n_ranges) * p.n_groups;
   return TMS_OK;
 }
