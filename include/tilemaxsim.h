@@ -42,6 +42,7 @@ extern "C" {
 #define TMS_ERR_CUDA 3        /* a CUDA runtime/driver call failed */
 #define TMS_ERR_TIMEOUT 4     /* a bounded device-side wait gave up (reported by tms_last_device_error) */
 #define TMS_ERR_WORKSPACE 5   /* workspace smaller than the *_workspace_size query */
+#define TMS_ERR_TOO_LARGE 6   /* problem needs more scratch than tms_dense_maxsim_noalloc holds */
 
 /* element types */
 #define TMS_F16 0
@@ -79,6 +80,23 @@ TMS_API int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int64_
                      const void* D, int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
                      int64_t nd_uniform, float* out, int out_mode, void* workspace,
                      size_t workspace_bytes, void* stream);
+
+/* No-allocation variant of tms_dense_maxsim. It has no counterpart in the reference.
+ * For callers that cannot hand the library any device memory -- e.g. a serving engine that
+ * reserves the whole GPU for its own memory pool at start-up, or a host plug-in that must not call
+ * cudaMalloc (which can synchronise the device and fail under memory pressure) -- the kernel's
+ * scratch lives in a fixed 4 MiB static device array that every GPU loading the library holds
+ * until exit. Same arguments and results as tms_dense_maxsim without the workspace; returns
+ * TMS_ERR_TOO_LARGE when tms_dense_workspace_size() for the problem exceeds 4 MiB (e.g. more than
+ * 512 queries of <= 32 tokens at d = 128 fp16). The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current) and caches it: make that first
+ * call before any stream capture. All calls share the one array, so two calls whose kernels
+ * overlap on the GPU race with each other; issue them on one stream (or otherwise order them).
+ * Nothing in the array has to start at zero. It allocates nothing and calls no allocator. */
+TMS_API int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_queries, int64_t nq,
+                                     int64_t d, const void* D, int64_t n_tokens,
+                                     const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                                     float* out, int out_mode, void* stream);
 
 /* ---------------------------------------------------------------- PQ asymmetric distance (ADC) */
 

@@ -20,6 +20,7 @@ TMS_ERR_UNSUPPORTED = 2
 TMS_ERR_CUDA = 3
 TMS_ERR_TIMEOUT = 4
 TMS_ERR_WORKSPACE = 5
+TMS_ERR_TOO_LARGE = 6
 
 TMS_F16, TMS_BF16, TMS_F32 = 0, 1, 2
 TMS_OUT_SCORE, TMS_OUT_TOKEN_MAX = 0, 1
@@ -36,6 +37,8 @@ SIGNATURES = {
     "tms_dense_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i32]),
     "tms_dense_maxsim": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _i32,
                                 _vp, _sz, _vp]),
+    "tms_dense_maxsim_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp,
+                                        _i32, _vp]),
     "tms_dense_plan_info": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i32, _i32,
                                    ctypes.POINTER(ctypes.c_int64)]),
     "tms_pq_table": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _vp]),

@@ -112,6 +112,7 @@ extern "C" const char* tms_strerror(int code) {
     case TMS_ERR_CUDA: return "CUDA error";
     case TMS_ERR_TIMEOUT: return "device wait timed out";
     case TMS_ERR_WORKSPACE: return "workspace too small";
+    case TMS_ERR_TOO_LARGE: return "problem exceeds the no-allocation entry point's static scratch";
     default: return "unknown error";
   }
 }

@@ -30,6 +30,7 @@
 // warps 2..5 = epilogue (lane quarter = warp % 4).
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "tms_device.cuh"
 #include "tms_internal.h"
@@ -829,4 +830,59 @@ extern "C" int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int
   info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_chunks_total == 1).total;
   info[9] = static_cast<int64_t>(p.n_ranges) * p.n_groups;
   return TMS_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// No-allocation variant of tms_dense_maxsim.
+//
+// Some callers cannot give this library device memory: a serving engine that reserves all of the
+// GPU's memory for its own pool at start-up and forbids other allocations, or a host plug-in that
+// must never call cudaMalloc (it can synchronise the whole device and fail under memory pressure)
+// and has no allocator of its own to pass in. For them the dense kernel's scratch -- the packed
+// query tiles and, for queries longer than 32 tokens, the per-chunk partial sums -- lives in the
+// fixed array below instead of a caller workspace. Every GPU that loads the library holds the
+// array until the process exits.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // usable scratch: 4 MiB per device
+constexpr size_t kNoAllocAlign = 1024;                     // the workspace alignment tms_dense_maxsim wants
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes + kNoAllocAlign];
+
+std::mutex g_noalloc_mutex;
+uint8_t* g_noalloc_base[64] = {};  // device address of the array, per device, 1024-aligned
+
+// Host code must not use the array's name as a device address: look the address up once per
+// device, with that device current, and cache it.
+int noalloc_scratch(uint8_t** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TMS_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return TMS_ERR_CUDA;
+    const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + kNoAllocAlign - 1) & ~(kNoAllocAlign - 1);
+    g_noalloc_base[dev] = reinterpret_cast<uint8_t*>(a);
+  }
+  *out = g_noalloc_base[dev];
+  return TMS_OK;
+}
+
+}  // namespace
+
+extern "C" int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_queries, int64_t nq,
+                                        int64_t d, const void* D, int64_t n_tokens,
+                                        const int64_t* doc_offsets, int64_t n_docs,
+                                        int64_t nd_uniform, float* out, int out_mode,
+                                        void* stream) {
+  // Nothing in the scratch has to start at zero: the pack kernel writes every byte of the query
+  // tiles (padding included) and every partial sum is written before it is read.
+  const size_t need = tms_dense_workspace_size(dtype, n_queries, nq, d, n_docs, out_mode);
+  if (need > kNoAllocScratchBytes) return TMS_ERR_TOO_LARGE;
+  uint8_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != TMS_OK) return rc;
+  return tms_dense_maxsim(Q, dtype, n_queries, nq, d, D, n_tokens, doc_offsets, n_docs, nd_uniform,
+                          out, out_mode, scratch, kNoAllocScratchBytes, stream);
 }
