@@ -59,7 +59,7 @@ def test_dense_workspace_query(d, ok):
 
 def test_dense_plans():
     """Launch plans on a 148-SM B200: single query -> one Q-resident group over all SMs;
-    64-query rerank -> 16 query tiles in groups of 2 over 144 CTAs; d=768 -> streaming mode."""
+    64-query rerank -> 16 query tiles in groups, CTAs a whole number of waves; d=768 -> streaming."""
     from tilemaxsim_b200 import _lib
     lib = _lib.load()
     info = (ctypes.c_int64 * 10)()
@@ -68,6 +68,6 @@ def test_dense_plans():
     assert (tn, qres, g, ng, nm, kc, ctas) == (256, 1, 1, 1, 1, 2, 148) and st >= 2 and smem <= 232448
     assert lib.tms_dense_plan_info(0, 64, 32, 128, 100_000, 18_000_000, 0, 148, info) == 0
     tn, qres, g, st, ng, nr, nm, kc, smem, ctas = list(info)
-    assert nm == 16 and qres == 1 and g * ng >= nm and ctas <= 148 and smem <= 232448
+    assert nm == 16 and qres == 1 and g * ng >= nm and ctas % 148 == 0 and smem <= 232448
     assert lib.tms_dense_plan_info(0, 16, 32, 768, 50_000, 12_800_000, 0, 148, info) == 0
     assert info[1] == 0 and info[8] <= 232448

@@ -83,7 +83,7 @@ __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G
   L.stage_off = q_bytes;
   L.stage_bytes = qres ? static_cast<uint32_t>(kc * TN * 128) : (kQChunkBytes + TN * 128u);
   L.bar_off = L.stage_off + static_cast<uint32_t>(stages) * L.stage_bytes;
-  const uint32_t n_bars = 2u * stages + 6u;
+  const uint32_t n_bars = 2u * stages + 2u * (512u / TN) + 2u;  // + accumulator slots, q, done
   L.carry_off = (L.bar_off + n_bars * 8u + 15u) & ~15u;
   L.x_off = L.carry_off + (split ? 0u : static_cast<uint32_t>(G) * kQTileRows * 4u);
   const uint32_t x_bytes =
@@ -150,10 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = a.stages;
   auto full_bar = [&](int s) { return bar_s + 8u * s; };
   auto empty_bar = [&](int s) { return bar_s + 8u * (S + s); };
+  constexpr int NSLOT = 512 / TN;  // TMEM accumulator slots (all 512 columns)
   auto accf_bar = [&](int b) { return bar_s + 8u * (2 * S + b); };
-  auto acce_bar = [&](int b) { return bar_s + 8u * (2 * S + 2 + b); };
-  const uint32_t qfull_bar = bar_s + 8u * (2 * S + 4);
-  const uint32_t done_bar = bar_s + 8u * (2 * S + 5);
+  auto acce_bar = [&](int b) { return bar_s + 8u * (2 * S + NSLOT + b); };
+  const uint32_t qfull_bar = bar_s + 8u * (2 * S + 2 * NSLOT);
+  const uint32_t done_bar = bar_s + 8u * (2 * S + 2 * NSLOT + 1);
   float* carry = reinterpret_cast<float*>(smem + L.carry_off);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
@@ -166,9 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_first = group * a.G;
   const int g_this = min(a.G, a.n_mtiles - m_first);
   // rows mode: the two epilogue groups take alternate query tiles (m parity). Only with an even
-  // number of tiles per CTA: then group g always owns TMEM slot g and waits on every phase of it
-  // in order (with an odd count a group would skip phases and a parity wait could match a stale
-  // completion two phases back).
+  // number of tiles per CTA: then the slot of unit u = t*g_this + m has the parity of m, so every
+  // TMEM slot belongs to one group, which waits on each of its phases in order (with an odd count
+  // a group would skip phases and a parity wait could match a stale completion two phases back).
   const bool two_groups = !split && g_this >= 2 && (g_this & 1) == 0;
 
   if (threadIdx.x == 0) {
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NSLOT; ++b) {
       mbar_init(accf_bar(b), 1);
       mbar_init(acce_bar(b), split ? kEpiWarps : 4);
     }
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * TN);
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -275,8 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         for (int m = 0; ok && m < g_this; ++m, ++u) {
-          const uint32_t slot = u & 1u;
-          if (!(ok = mbar_wait(acce_bar(slot), ((u >> 1) & 1u) ^ 1u, abort_flag, tmo, a.err, 5)))
+          const uint32_t slot = u % NSLOT;
+          if (!(ok = mbar_wait(acce_bar(slot), ((u / NSLOT) & 1u) ^ 1u, abort_flag, tmo, a.err, 5)))
             break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + slot * TN;
@@ -355,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     auto wait_full = [&](uint32_t slot, uint32_t uu) -> bool {
       int w = 0;
-      if (lane == 0) w = mbar_wait(accf_bar(slot), (uu >> 1) & 1u, abort_flag, tmo, a.err, 8);
+      if (lane == 0) w = mbar_wait(accf_bar(slot), (uu / NSLOT) & 1u, abort_flag, tmo, a.err, 8);
       return __shfl_sync(0xffffffffu, w, 0) != 0;
     };
     const bool skip_math = (a.debug_flags & 4) != 0;
@@ -375,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int kParts = TN / 32;
       float running = kNegInf;  // combine warp: max of the document open at the last part's end
       for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN, ++u) {
-        const uint32_t slot = u & 1u;
+        const uint32_t slot = u % NSLOT;
         const bool w_ok = wait_full(slot, u);
         tc_fence_after();
         const int ncol = (tok_hi - t0 < TN) ? static_cast<int>(tok_hi - t0) : TN;
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int64_t next_doc = doc, next_dend = dend;
         for (int m = 0; m < g_this; ++m, ++u) {
           if (two_groups && (m & 1) != eg) continue;
-          const uint32_t slot = u & 1u;
+          const uint32_t slot = u % NSLOT;
           if (!(ok = wait_full(slot, u))) break;
           tc_fence_after();
           const int chunk = (m_first + m) * 4 + lg;
@@ -493,33 +494,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             int dcol = rel(de);
             const uint32_t tbase = t_lane + slot * TN;
-            uint32_t ra[32], rb[32];
-            tmem_ld32_async(tbase, ra);
-#pragma unroll
-            for (int b = 0; b < TN / 32; ++b) {
-              uint32_t(&cur)[32] = (b & 1) ? rb : ra;
-              uint32_t(&nxt)[32] = (b & 1) ? ra : rb;
-              const int cb = 32 * b;
-              if (cb < ncol) {
-                tmem_wait_ld32(cur);
-                if (b + 1 < TN / 32 && cb + 32 < ncol) tmem_ld32_async(tbase + cb + 32, nxt);
-                if (dcol >= cb + 32 && ncol >= cb + 32) {
-                  rm = max32(rm, cur);  // the whole block lies in the open document
-                } else {
-                  const int n = (ncol - cb < 32) ? ncol - cb : 32;
-                  int lo = 0;
-                  while (true) {
-                    const int hi = (dcol - cb < n) ? dcol - cb : n;
-                    rm = range_max32(rm, cur, lo, hi);
-                    if (dcol - cb >= n) break;
-                    emit(chunk, dd, rm);
-                    rm = kNegInf;
-                    ++dd;
-                    de = doc_end(dd);
-                    dcol = rel(de);
-                    lo = hi;
-                  }
+            // 32 columns starting at column cb, all < ncol
+            auto reduce32 = [&](const uint32_t(&v)[32], int cb) {
+              if (dcol >= cb + 32 && ncol >= cb + 32) {
+                rm = max32(rm, v);  // the whole block lies in the open document
+              } else {
+                const int n = (ncol - cb < 32) ? ncol - cb : 32;
+                int lo = 0;
+                while (true) {
+                  const int hi = (dcol - cb < n) ? dcol - cb : n;
+                  rm = range_max32(rm, v, lo, hi);
+                  if (dcol - cb >= n) break;
+                  emit(chunk, dd, rm);
+                  rm = kNegInf;
+                  ++dd;
+                  de = doc_end(dd);
+                  dcol = rel(de);
+                  lo = hi;
                 }
+              }
+            };
+            // 64-column TMEM loads, double-buffered: block b+1 is in flight while b is reduced
+            uint32_t ra[64], rb[64];
+            tmem_ld64_async(tbase, ra);
+#pragma unroll
+            for (int b = 0; b < TN / 64; ++b) {
+              uint32_t(&cur)[64] = (b & 1) ? rb : ra;
+              uint32_t(&nxt)[64] = (b & 1) ? ra : rb;
+              const int cb = 64 * b;
+              if (cb < ncol) {
+                tmem_wait_ld(cur);
+                if (b + 1 < TN / 64 && cb + 64 < ncol) tmem_ld64_async(tbase + cb + 64, nxt);
+                reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[0]), cb);
+                if (cb + 32 < ncol) reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[32]), cb + 32);
               }
             }
             carry[m * kQTileRows + row] = rm;
@@ -554,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * TN);
+    tmem_dealloc(tmem_base, 512);
   }
 }
 
@@ -626,6 +633,8 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
                          : 0;
 
   const int budget = max_smem - 2560 - 64;  // barriers, carries / exchange area, misc
+  // 256-token tiles: M=128 x N=256 MMAs stay under the shared-memory read bandwidth (N=128 with
+  // both operands in shared memory does not), at the cost of 2 TMEM accumulator slots.
   p->TN = static_cast<int>(env_int("TMS_DENSE_TN", p->kc <= 2 ? 256 : 128));
   if (p->TN != 128 && p->TN != 256) p->TN = 256;
   const int stage_d = p->kc * p->TN * 128;
@@ -664,7 +673,12 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   const SmemLayout L =
       dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages, p->n_chunks_total == 1);
   if (static_cast<int>(L.total) > max_smem) return TMS_ERR_UNSUPPORTED;
-  int64_t ranges = p->n_groups >= num_sms ? 1 : num_sms / p->n_groups;
+  // Token ranges per query group: the fewest that make groups x ranges a multiple of the SM count
+  // (one balanced wave or several), but never fewer than fill one wave.
+  int64_t gcd = num_sms, gb = p->n_groups;
+  while (gb) { const int64_t t = gcd % gb; gcd = gb; gb = t; }
+  int64_t ranges = num_sms / gcd;
+  if (p->n_groups < num_sms && ranges < num_sms / p->n_groups) ranges = num_sms / p->n_groups;
   ranges = env_int("TMS_DENSE_RANGES", ranges);
   const int64_t tiles = (n_tokens + p->TN - 1) / p->TN;
   if (ranges > tiles) ranges = tiles;
