@@ -49,6 +49,10 @@ extern "C" {
 #define TMS_BF16 1
 #define TMS_F32 2 /* multiplied as TF32 on the tensor cores, like the reference's tl.dot on fp32 */
 
+/* PQ modes */
+#define TMS_PQ_FAST 0  /* tensor cores where the shape allows (default) */
+#define TMS_PQ_EXACT 1 /* fp32 table lookups */
+
 /* dense output modes */
 #define TMS_OUT_SCORE 0     /* out[q * n_docs + doc] = sum_i max_j <Q_qi, D_j>                 */
 #define TMS_OUT_TOKEN_MAX 1 /* out[(q * n_docs + doc) * nq + i] = max_j <Q_qi, D_j> (V1 output) */
@@ -105,15 +109,21 @@ TMS_API int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_queries
 TMS_API int tms_pq_table(const void* Q, int q_dtype, int64_t n_queries, int64_t nq, const void* codebook,
                  int cb_dtype, int64_t M, int64_t K, int64_t dsub, float* table, void* stream);
 
-TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K, int64_t n_docs);
+TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K,
+                                     int64_t dsub, int64_t n_docs);
 
 /* codes: (n_tokens, M) uint8, doc layout as in tms_dense_maxsim (offsets or nd_uniform).
- * out[q * n_docs + doc] = sum_i max_j sum_m table[q,i,m,codes[j,m]]; the distance table is built in
- * shared memory from Q and the codebook inside the kernel (K <= 256). */
-TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq, const void* codebook,
-                  int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
-                  int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
-                  float* out, void* workspace, size_t workspace_bytes, void* stream);
+ * out[q * n_docs + doc] = sum_i max_j sum_m table[q,i,m,codes[j,m]] (K <= 256).
+ * mode TMS_PQ_FAST: fp16 queries with dsub % 8 == 0, M*dsub % 64 == 0 and a codebook of <= 96 KB
+ * in fp16 run on the tensor cores (codes decoded in shared memory through the codebook rounded to
+ * fp16, never written to HBM; |error| <= 1e-3*|score| + 5e-3); other shapes fall back to:
+ * mode TMS_PQ_EXACT: the fp32 distance table is built in shared memory and table entries are
+ * summed in m order (the reference's arithmetic). The workspace must be 1024-byte aligned. */
+TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
+                          const void* codebook, int cb_dtype, int64_t M, int64_t K, int64_t dsub,
+                          const uint8_t* codes, int64_t n_tokens, const int64_t* doc_offsets,
+                          int64_t n_docs, int64_t nd_uniform, float* out, int mode,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- top-k */
 

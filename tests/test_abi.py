@@ -44,7 +44,8 @@ def test_invalid_arguments_rejected_without_gpu():
     # nothing to do is OK
     assert lib.tms_dense_maxsim(nul, 0, 0, 32, 128, nul, 10, nul, 1, 10, nul, 0, nul, 0, nul) == _lib.TMS_OK
     assert lib.tms_topk(nul, 1, 10, 5, 3, nul, 0, 0, nul, nul, nul, 0, nul) == _lib.TMS_ERR_INVALID  # ld < n
-    assert lib.tms_pq_maxsim(nul, 0, 1, 32, nul, 2, 16, 300, 8, nul, 0, nul, 1, 0, nul, nul, 0, nul) == _lib.TMS_ERR_UNSUPPORTED
+    assert lib.tms_pq_maxsim(nul, 0, 1, 32, nul, 2, 16, 300, 8, nul, 0, nul, 1, 0, nul, 0, nul, 0, nul) == _lib.TMS_ERR_UNSUPPORTED
+    assert lib.tms_pq_maxsim(nul, 0, 1, 32, nul, 2, 16, 256, 8, nul, 0, nul, 1, 0, nul, 7, nul, 0, nul) == _lib.TMS_ERR_INVALID
 
 
 @pytest.mark.parametrize("d,ok", [(128, True), (64, True), (768, True), (96, True), (100, False)])

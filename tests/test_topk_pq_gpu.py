@@ -49,36 +49,61 @@ def test_topk_merge_with_ids(cuda_device):
     np.testing.assert_array_equal(vals.cpu().numpy(), wv)
 
 
+PATHS = ["tensor", "exact"]  # tensor-core decode path (default) / fp32 table-lookup path
+# tensor path: codebook rounded to fp16 -> |error| <= 1e-3*|score| + 5e-3; exact path: 1e-3 + 1e-3
+TOL = {"tensor": (1e-3, 5e-3), "exact": (1e-3, 1e-3)}
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name,cb_dtype", [("pq_f32", torch.float32), ("pq_f16", torch.float16)])
-def test_pq_golden(name, cb_dtype, cuda_device):
+def test_pq_golden(name, cb_dtype, path, cuda_device):
+    rtol, atol = TOL[path]
     from tilemaxsim_b200 import TileMaxSimPQ
     _, g = load_golden(name)
     c = R.pq_case(cb_dtype)
-    pq = TileMaxSimPQ(c["codebook"].to(cuda_device))
+    pq = TileMaxSimPQ(c["codebook"].to(cuda_device), exact=(path == "exact"))
     Q, codes = c["Q"].to(cuda_device), c["codes"].to(cuda_device)
     got = pq.score_batch(Q, codes).cpu().numpy()
-    np.testing.assert_allclose(got, g["adc"], rtol=1e-3, atol=1e-3)
-    np.testing.assert_allclose(got, g["decompress"], rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(got, g["adc"], rtol=rtol, atol=atol)
+    np.testing.assert_allclose(got, g["decompress"], rtol=rtol, atol=atol)
     s1 = pq.score_single(Q, codes[3])
     assert s1.dim() == 0
-    np.testing.assert_allclose(s1.item(), g["adc"][3], rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(s1.item(), g["adc"][3], rtol=rtol, atol=atol)
     T = pq.build_distance_table(Q).cpu().numpy()
     np.testing.assert_allclose(T, O.pq_table(c["Q"], c["codebook"]), rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("M,K,dsub,nq", [(16, 256, 8, 32), (8, 256, 16, 32), (32, 256, 4, 32),
-                                         (16, 100, 8, 5), (12, 256, 8, 40)])
-def test_pq_ragged_multiquery(M, K, dsub, nq, cuda_device):
+                                         (16, 100, 8, 5), (12, 256, 8, 40), (16, 256, 8, 1),
+                                         (32, 256, 8, 64)])
+def test_pq_ragged_multiquery(M, K, dsub, nq, path, cuda_device):
+    rtol, atol = TOL[path]
     from tilemaxsim_b200 import TileMaxSimPQ
     lengths = R.ragged_lengths(400, 0, 200, seed=M + K)
     off = R.offsets_from_lengths(lengths)
     cb = R.randn((M, K, dsub), 3, torch.float32)
-    Qb = R.normalized((3, nq, M * dsub), 4)
+    Qb = R.normalized((5, nq, M * dsub), 4)
     codes = torch.randint(0, K, (int(off[-1]), M), generator=R.gen(5), dtype=torch.uint8)
-    pq = TileMaxSimPQ(cb.to(cuda_device))
+    pq = TileMaxSimPQ(cb.to(cuda_device), exact=(path == "exact"))
     got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device), torch.from_numpy(off).to(cuda_device))
     want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
     got = got.cpu().numpy()
     inf = np.isinf(want)
     np.testing.assert_array_equal(got[inf], want[inf])
-    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=rtol, atol=atol)
+
+
+def test_pq_tensor_path_full_size_property(cuda_device):
+    """BASELINE config 4 shape on a 200k-document slice (25.6M code rows): the tensor-core path
+    agrees with the exact table-lookup path on every score (1e-3 relative + 5e-3)."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    n, nd = 200_000, 128
+    codes = torch.randint(0, 256, (n * nd, 16), generator=g, device=cuda_device, dtype=torch.uint8)
+    off = torch.arange(n + 1, device=cuda_device, dtype=torch.int64) * nd
+    cb = torch.randn(16, 256, 8, generator=g, device=cuda_device)
+    Qb = torch.nn.functional.normalize(torch.randn(16, 32, 128, generator=g, device=cuda_device), dim=-1).half()
+    fast = TileMaxSimPQ(cb).score_queries(Qb, codes, off)
+    exact = TileMaxSimPQ(cb, exact=True).score_queries(Qb, codes, off)
+    torch.testing.assert_close(fast, exact, rtol=1e-3, atol=5e-3)

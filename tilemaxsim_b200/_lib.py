@@ -24,6 +24,7 @@ TMS_ERR_TOO_LARGE = 6
 
 TMS_F16, TMS_BF16, TMS_F32 = 0, 1, 2
 TMS_OUT_SCORE, TMS_OUT_TOKEN_MAX = 0, 1
+TMS_PQ_FAST, TMS_PQ_EXACT = 0, 1
 
 DTYPE_CODE = {torch.float16: TMS_F16, torch.bfloat16: TMS_BF16, torch.float32: TMS_F32}
 
@@ -42,9 +43,9 @@ SIGNATURES = {
     "tms_dense_plan_info": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i32, _i32,
                                    ctypes.POINTER(ctypes.c_int64)]),
     "tms_pq_table": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _vp]),
-    "tms_pq_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "tms_pq_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "tms_pq_maxsim": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64,
-                             _i64, _vp, _vp, _sz, _vp]),
+                             _i64, _vp, _i32, _vp, _sz, _vp]),
     "tms_topk_workspace_size": (_sz, [_i64, _i64, _i64]),
     "tms_topk": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _sz, _vp]),
 }

@@ -26,11 +26,15 @@
 //  * Q-resident mode keeps the CTA's G query tiles in shared memory for the whole range; streaming
 //    mode (large d) loads one (query chunk, doc chunk) pair per pipeline stage.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
-// warps 2..5 = epilogue (lane quarter = warp % 4).
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2..9 = epilogue (lane quarter = warp % 4). The PQ variant adds warps 10..13, which decode
+// uint8 codes through a shared-memory fp16 codebook into the D stages instead of a TMA load.
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "tms_device.cuh"
 #include "tms_internal.h"
@@ -39,7 +43,9 @@ namespace tms {
 
 namespace {
 
-constexpr int kThreads = 320;  // 2 control warps + 8 epilogue warps
+constexpr int kThreads = 320;    // 2 control warps + 8 epilogue warps
+constexpr int kPqThreadsMma = 448;  // + 4 decoder warps (PQ variant)
+constexpr int kDecodeWarp0 = 10;
 constexpr int kEpiWarps = 8;
 constexpr int kQTileRows = 128;
 constexpr uint32_t kQChunkBytes = kQTileRows * 128;  // one 128-row x 128-byte K chunk of Q
@@ -61,6 +67,11 @@ struct DenseArgs {
   int stages;
   int out_mode;
   uint32_t ab_format;  // MMA operand format: 0 = f16, 1 = bf16, 2 = tf32
+  // PQ variant: D rows are decoded from codes (n_tokens, M) through codebook (M, K, dsub)
+  const uint8_t* codes;
+  const void* codebook;
+  int cb_dtype, pq_M, pq_K, pq_dsub;
+  uint32_t cb_bytes;   // fp16 codebook bytes staged in shared memory (0 for the dense kernel)
   int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits);
                        // bits 2/3: skip the epilogue math / the MMAs (timing experiments only)
 };
@@ -68,7 +79,7 @@ struct DenseArgs {
 // Shared-memory carve-up, identical on host and device. `split` (one query of <= 32 tokens) adds
 // the exchange area of the column-split epilogue and drops the per-row carries.
 struct SmemLayout {
-  uint32_t q_off, stage_off, stage_bytes, bar_off, carry_off, x_off, misc_off, total;
+  uint32_t q_off, stage_off, stage_bytes, bar_off, carry_off, x_off, cb_off, misc_off, total;
 };
 struct PartMeta {  // one epilogue warp's summary of its column part (split mode)
   int64_t head_doc;  // document whose end lies in the part (valid if has_b)
@@ -76,7 +87,8 @@ struct PartMeta {  // one epilogue warp's summary of its column part (split mode
   int32_t has_b, pad;
 };
 __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G, int kc,
-                                                        int stages, bool split) {
+                                                        int stages, bool split,
+                                                        uint32_t cb_bytes = 0) {
   SmemLayout L;
   L.q_off = 0;
   const uint32_t q_bytes = qres ? static_cast<uint32_t>(G * kc) * kQChunkBytes : 0u;
@@ -88,7 +100,8 @@ __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G
   L.x_off = L.carry_off + (split ? 0u : static_cast<uint32_t>(G) * kQTileRows * 4u);
   const uint32_t x_bytes =
       split ? 2u * kEpiWarps * 32u * 4u + kEpiWarps * static_cast<uint32_t>(sizeof(PartMeta)) : 0u;
-  L.misc_off = (L.x_off + x_bytes + 15u) & ~15u;
+  L.cb_off = (L.x_off + x_bytes + 15u) & ~15u;
+  L.misc_off = (L.cb_off + cb_bytes + 15u) & ~15u;
   L.total = L.misc_off + 64u;
   return L;
 }
@@ -136,13 +149,13 @@ __device__ __forceinline__ float range_max32(float acc, const uint32_t (&r)[32],
   return fmaxf(m0, m1);
 }
 
-template <int TN, bool QRES, bool TF32>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int TN, bool QRES, bool TF32, bool PQ>
+__global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const bool split = a.n_chunks_total == 1;  // one query: column-split epilogue
-  const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages, split);
+  const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages, split, a.cb_bytes);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t q_s = sbase + L.q_off;
   const uint32_t st_s = sbase + L.stage_off;
@@ -174,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1);
+      mbar_init(full_bar(s), PQ ? 4 : 1);  // PQ: one arrival per decoder warp
       mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < NSLOT; ++b) {
@@ -204,6 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       rinfo->tok_hi = (doc_hi > doc_lo) ? a.docs.start(doc_hi) : a.docs.start(doc_lo);
       prefetch_tmap(&dmap);
       prefetch_tmap(&qmap);
+    }
+  }
+  if (PQ) {  // stage the codebook in shared memory as fp16 (every thread helps)
+    __half* cbs = reinterpret_cast<__half*>(smem + L.cb_off);
+    const int n = a.pq_M * a.pq_K * a.pq_dsub;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float v;
+      if (a.cb_dtype == TMS_F16) v = __half2float(reinterpret_cast<const __half*>(a.codebook)[i]);
+      else if (a.cb_dtype == TMS_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.codebook)[i]);
+      else v = reinterpret_cast<const float*>(a.codebook)[i];
+      cbs[i] = __float2half_rn(v);
     }
   }
   if (warp == 1) {
@@ -237,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int s = 0;
       uint32_t ph = 0;
-      bool ok = true;
+      bool ok = !PQ;  // the PQ variant's D stages are filled by the decoder warps
       for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
         if (QRES) {
           if (!(ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 1))) break;
@@ -261,6 +285,79 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+    }
+  } else if (PQ && warp >= kDecodeWarp0) {
+    // ------------------------------------------------------------------ PQ decoders
+    // Row r of a D stage = token t0 + r rebuilt from its M codes: codebook row (m, code) is
+    // dsub fp16 values = dsub/8 16-byte units, placed at columns m*dsub.. of the row in the
+    // 128-byte-swizzle layout the MMA descriptors expect (unit u of row r at u ^ (r % 8)).
+    const __half* cbs = reinterpret_cast<const __half*>(smem + L.cb_off);
+    const int dt = threadIdx.x - kDecodeWarp0 * 32;  // 0..127
+    const int M = a.pq_M, K = a.pq_K, dsub = a.pq_dsub;
+    const bool m16 = (M == 16) && ((reinterpret_cast<uintptr_t>(a.codes) & 15) == 0);
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = !(a.debug_flags & 1);
+    constexpr int TPT = TN / 128;  // tokens per decoder thread per tile
+    // Codes of the common shape are prefetched two tiles ahead in registers, so the HBM latency of
+    // a tile's codes overlaps the decoding of the tiles before it.
+    auto load_codes = [&](int64_t t0, uint4 (&c)[TPT]) {
+#pragma unroll
+      for (int i = 0; i < TPT; ++i) {
+        const int64_t tok = t0 + dt + 128 * i;
+        c[i] = (m16 && dsub == 8 && tok < tok_hi)
+                   ? __ldg(reinterpret_cast<const uint4*>(a.codes + tok * 16))
+                   : make_uint4(0, 0, 0, 0);
+      }
+    };
+    uint4 c_cur[TPT], c_n1[TPT], c_n2[TPT];
+    load_codes(tok_lo, c_n1);
+    load_codes(tok_lo + TN, c_n2);
+    for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+#pragma unroll
+      for (int i = 0; i < TPT; ++i) {
+        c_cur[i] = c_n1[i];
+        c_n1[i] = c_n2[i];
+      }
+      load_codes(t0 + 2 * TN, c_n2);
+      int w = 0;
+      if (lane == 0) w = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 9);
+      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+      uint8_t* st = smem + L.stage_off + static_cast<size_t>(s) * L.stage_bytes;
+#pragma unroll
+      for (int i = 0; i < TPT; ++i) {
+        const int r = dt + 128 * i;
+        const int64_t tok = t0 + r;
+        if (tok >= tok_hi) continue;  // columns past the range are never read by the epilogue
+        const uint8_t* crow = a.codes + tok * M;
+        uint8_t* rowp = st + r * 128;
+        const uint32_t sw = static_cast<uint32_t>(r & 7);
+        if (m16 && dsub == 8) {
+          // common shape (M = 16, dsub = 8, d = 128): 16 unrolled 16-byte copies
+          const uint32_t cw[4] = {c_cur[i].x, c_cur[i].y, c_cur[i].z, c_cur[i].w};
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            uint32_t code = (cw[m >> 2] >> (8 * (m & 3))) & 0xffu;
+            code = min(code, static_cast<uint32_t>(K - 1));  // never read past the codebook
+            const uint4 v = *reinterpret_cast<const uint4*>(cbs + (m * K + code) * 8);
+            *reinterpret_cast<uint4*>(rowp + (m >> 3) * (TN * 128) + (((m & 7) ^ sw) << 4)) = v;
+          }
+        } else {
+          for (int m = 0; m < M; ++m) {
+            const uint32_t code = min(static_cast<uint32_t>(__ldg(crow + m)), static_cast<uint32_t>(K - 1));
+            const uint4* src = reinterpret_cast<const uint4*>(cbs + (m * K + code) * dsub);
+            for (int h = 0; h < dsub; h += 8) {
+              const int col = m * dsub + h;
+              const uint32_t u = static_cast<uint32_t>((col & 63) >> 3);
+              *reinterpret_cast<uint4*>(rowp + (col >> 6) * (TN * 128) + ((u ^ sw) << 4)) = src[h >> 3];
+            }
+          }
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full_bar(s));
+      if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -514,19 +611,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
             };
-            // 64-column TMEM loads, double-buffered: block b+1 is in flight while b is reduced
-            uint32_t ra[64], rb[64];
-            tmem_ld64_async(tbase, ra);
+            // TMEM loads double-buffered (block b+1 in flight while b is reduced): 64 columns
+            // per load, 32 in the PQ variant (448 threads leave it fewer registers)
+            if constexpr (!PQ) {
+              uint32_t ra[64], rb[64];
+              tmem_ld64_async(tbase, ra);
 #pragma unroll
-            for (int b = 0; b < TN / 64; ++b) {
-              uint32_t(&cur)[64] = (b & 1) ? rb : ra;
-              uint32_t(&nxt)[64] = (b & 1) ? ra : rb;
-              const int cb = 64 * b;
-              if (cb < ncol) {
-                tmem_wait_ld(cur);
-                if (b + 1 < TN / 64 && cb + 64 < ncol) tmem_ld64_async(tbase + cb + 64, nxt);
-                reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[0]), cb);
-                if (cb + 32 < ncol) reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[32]), cb + 32);
+              for (int b = 0; b < TN / 64; ++b) {
+                uint32_t(&cur)[64] = (b & 1) ? rb : ra;
+                uint32_t(&nxt)[64] = (b & 1) ? ra : rb;
+                const int cb = 64 * b;
+                if (cb < ncol) {
+                  tmem_wait_ld(cur);
+                  if (b + 1 < TN / 64 && cb + 64 < ncol) tmem_ld64_async(tbase + cb + 64, nxt);
+                  reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[0]), cb);
+                  if (cb + 32 < ncol) reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[32]), cb + 32);
+                }
+              }
+            } else {
+              uint32_t ra[32], rb[32];
+              tmem_ld32_async(tbase, ra);
+#pragma unroll
+              for (int b = 0; b < TN / 32; ++b) {
+                uint32_t(&cur)[32] = (b & 1) ? rb : ra;
+                uint32_t(&nxt)[32] = (b & 1) ? ra : rb;
+                const int cb = 32 * b;
+                if (cb < ncol) {
+                  tmem_wait_ld32(cur);
+                  if (b + 1 < TN / 32 && cb + 32 < ncol) tmem_ld32_async(tbase + cb + 32, nxt);
+                  reduce32(cur, cb);
+                }
               }
             }
             carry[m * kQTileRows + row] = rm;
@@ -612,10 +726,13 @@ struct DensePlan {
   int TN, G, stages, n_groups, n_ranges;
   bool qres;
   size_t qp_bytes, partial_bytes;
+  uint32_t cb_bytes;
 };
 
 int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs,
-               int64_t n_tokens, int out_mode, int num_sms, int max_smem, DensePlan* p) {
+               int64_t n_tokens, int out_mode, int num_sms, int max_smem, DensePlan* p,
+               uint32_t cb_bytes = 0, int prefer_tn = 0) {
+  p->cb_bytes = cb_bytes;
   p->esize = (dtype == TMS_F32) ? 4 : 2;
   p->cw = 128 / p->esize;
   if ((d * p->esize) % 16 != 0) return TMS_ERR_UNSUPPORTED;
@@ -632,15 +749,17 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
                          ? align_up(static_cast<size_t>(chunks) * n_docs * 4, 256)
                          : 0;
 
-  const int budget = max_smem - 2560 - 64;  // barriers, carries / exchange area, misc
+  // barriers, carries / exchange area, misc, and the PQ variant's codebook
+  const int budget = max_smem - 2560 - 64 - static_cast<int>(align_up(cb_bytes, 16));
   // 256-token tiles: M=128 x N=256 MMAs stay under the shared-memory read bandwidth (N=128 with
   // both operands in shared memory does not), at the cost of 2 TMEM accumulator slots.
-  p->TN = static_cast<int>(env_int("TMS_DENSE_TN", p->kc <= 2 ? 256 : 128));
+  p->TN = static_cast<int>(env_int("TMS_DENSE_TN", prefer_tn ? prefer_tn : (p->kc <= 2 ? 256 : 128)));
   if (p->TN != 128 && p->TN != 256) p->TN = 256;
   const int stage_d = p->kc * p->TN * 128;
   const int qtile = p->kc * static_cast<int>(kQChunkBytes);
   const bool force_stream = env_int("TMS_DENSE_STREAM", 0) != 0;
   p->qres = !force_stream && (qtile + 2 * stage_d <= budget);
+  if (cb_bytes && !p->qres) return TMS_ERR_UNSUPPORTED;  // the PQ variant keeps Q resident
   if (p->qres) {
     int gmax = (budget - 2 * stage_d) / qtile;
     gmax = static_cast<int>(env_int("TMS_DENSE_G", gmax < 4 ? gmax : 4));
@@ -670,8 +789,8 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
   }
   if (p->stages < 1) p->stages = 1;
-  const SmemLayout L =
-      dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages, p->n_chunks_total == 1);
+  const SmemLayout L = dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages,
+                                        p->n_chunks_total == 1, p->cb_bytes);
   if (static_cast<int>(L.total) > max_smem) return TMS_ERR_UNSUPPORTED;
   // Token ranges per query group: the fewest that make groups x ranges a multiple of the SM count
   // (one balanced wave or several), but never fewer than fill one wave.
@@ -689,16 +808,17 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   return TMS_OK;
 }
 
-template <int TN, bool QRES, bool TF32>
+template <int TN, bool QRES, bool TF32, bool PQ = false>
 int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
                    const DensePlan& p, cudaStream_t st) {
-  auto kern = dense_maxsim_kernel<TN, QRES, TF32>;
-  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_chunks_total == 1);
+  auto kern = dense_maxsim_kernel<TN, QRES, TF32, PQ>;
+  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_chunks_total == 1,
+                                         p.cb_bytes);
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (e != cudaSuccess) return TMS_ERR_CUDA;
   const unsigned grid = static_cast<unsigned>(p.n_ranges) * static_cast<unsigned>(p.n_groups);
-  kern<<<grid, kThreads, L.total, st>>>(qm, dm, args);
+  kern<<<grid, PQ ? kPqThreadsMma : kThreads, L.total, st>>>(qm, dm, args);
   return cuda_status(cudaGetLastError());
 }
 
@@ -812,6 +932,10 @@ extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int
   args.stages = p.stages;
   args.out_mode = out_mode;
   args.ab_format = (dtype == TMS_F16) ? 0u : (dtype == TMS_BF16) ? 1u : 2u;
+  args.codes = nullptr;
+  args.codebook = nullptr;
+  args.cb_dtype = args.pq_M = args.pq_K = args.pq_dsub = 0;
+  args.cb_bytes = 0;
   args.debug_flags = debug_flags();
 
   rc = launch_dense(qm, dm, args, p, dtype == TMS_F32, st);
@@ -841,10 +965,99 @@ extern "C" int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int
   info[5] = p.n_ranges;
   info[6] = p.n_mtiles;
   info[7] = p.kc;
-  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_chunks_total == 1).total;
+  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_chunks_total == 1, 0).total;
   info[9] = static_cast<int64_t>(p.n_ranges) * p.n_groups;
   return TMS_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// PQ-ADC on the tensor cores: the dense kernel with decoder warps (see the kernel's PQ branch).
+// ------------------------------------------------------------------------------------------------
+namespace tms {
+
+// fp16 codebook bytes if the tensor-core PQ path can take this shape, else 0.
+size_t pq_mma_codebook_bytes(int64_t M, int64_t K, int64_t dsub) {
+  const int64_t d = M * dsub;
+  if (K < 1 || K > 256 || dsub % 8 != 0 || d % 64 != 0 || d > 512) return 0;
+  const int64_t b = M * K * dsub * 2;
+  return b <= 96 * 1024 ? static_cast<size_t>(b) : 0;
+}
+
+size_t pq_mma_workspace_size(int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs) {
+  return tms_dense_workspace_size(TMS_F16, n_queries, nq, d, n_docs, TMS_OUT_SCORE);
+}
+
+int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook, int cb_dtype,
+                  int64_t M, int64_t K, int64_t dsub, const uint8_t* codes, int64_t n_tokens,
+                  const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const size_t cb_bytes = pq_mma_codebook_bytes(M, K, dsub);
+  if (!cb_bytes || n_tokens <= 0 || n_tokens >= (int64_t(1) << 31)) return TMS_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(Q) & 15) return TMS_ERR_UNSUPPORTED;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  const int64_t d = M * dsub;
+  DensePlan p;
+  int rc = plan_dense(TMS_F16, n_queries, nq, d, n_docs, n_tokens, TMS_OUT_SCORE, dev->num_sms,
+                      dev->max_smem_optin, &p, static_cast<uint32_t>(cb_bytes),
+                      /* 128-token tiles: two query tiles per CTA fit beside the codebook */ 128);
+  if (rc != TMS_OK) return rc;
+  if (!workspace || workspace_bytes < p.qp_bytes + p.partial_bytes) return TMS_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 1023) return TMS_ERR_INVALID;
+  uint8_t* qp = static_cast<uint8_t*>(workspace);
+  float* partial = reinterpret_cast<float*>(qp + p.qp_bytes);
+  const int row_bytes = static_cast<int>(d * 2);
+  const int vpr = row_bytes / 16;
+  const int64_t n_vec = static_cast<int64_t>(p.n_mtiles) * kQTileRows * vpr;
+  int blocks = static_cast<int>((n_vec + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  pack_query_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(Q),
+                                                  reinterpret_cast<uint4*>(qp), n_vec, vpr,
+                                                  static_cast<int>(nq), p.nchunk, p.n_chunks_total,
+                                                  p.n_chunks_total == 1);
+  if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
+  CUtensorMap qm;
+  rc = encode_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qp, static_cast<uint64_t>(d),
+                      static_cast<uint64_t>(p.n_mtiles) * kQTileRows, row_bytes, p.cw, kQTileRows);
+  if (rc != TMS_OK) return rc;
+  DenseArgs args;
+  args.docs.offsets = doc_offsets;
+  args.docs.n_docs = n_docs;
+  args.docs.nd = doc_offsets ? 0 : nd_uniform;
+  args.out = p.nchunk > 1 ? partial : out;
+  args.err = dev->err_word;
+  args.timeout_ns = wait_timeout_ns();
+  args.n_chunks_total = p.n_chunks_total;
+  args.nchunk = p.nchunk;
+  args.nq = static_cast<int>(nq);
+  args.n_mtiles = p.n_mtiles;
+  args.G = p.G;
+  args.n_groups = p.n_groups;
+  args.n_ranges = p.n_ranges;
+  args.kc = p.kc;
+  args.stages = p.stages;
+  args.out_mode = TMS_OUT_SCORE;
+  args.ab_format = 0u;
+  args.codes = codes;
+  args.codebook = codebook;
+  args.cb_dtype = cb_dtype;
+  args.pq_M = static_cast<int>(M);
+  args.pq_K = static_cast<int>(K);
+  args.pq_dsub = static_cast<int>(dsub);
+  args.cb_bytes = static_cast<uint32_t>(cb_bytes);
+  args.debug_flags = debug_flags() & 1;
+  rc = (p.TN == 256) ? launch_dense_t<256, true, false, true>(qm, qm, args, p, st)
+                     : launch_dense_t<128, true, false, true>(qm, qm, args, p, st);
+  if (rc != TMS_OK || p.nchunk == 1) return rc;
+  const int64_t total = n_queries * n_docs;
+  blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  sum_query_chunks_kernel<<<blocks, 256, 0, st>>>(partial, out, n_queries, n_docs, p.nchunk);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace tms
 
 // ------------------------------------------------------------------------------------------------
 // No-allocation variant of tms_dense_maxsim.

@@ -206,19 +206,38 @@ extern "C" int tms_pq_table(const void* Q, int q_dtype, int64_t n_queries, int64
   return cuda_status(cudaGetLastError());
 }
 
-extern "C" size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K,
-                                        int64_t n_docs) {
-  if (n_queries <= 0 || nq <= 0 || M <= 0 || K <= 0 || n_docs < 0) return 0;
+namespace {
+size_t pq_lut_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K, int64_t n_docs) {
   const int qs = pick_qs(M, K, nq);
   const int64_t nslice = (nq + qs - 1) / qs;
   return nslice > 1 ? static_cast<size_t>(n_queries * nslice * n_docs) * 4 : 0;
+}
+// Both paths need at most this much (the tensor-core path's packed query tiles + partials, or the
+// table-lookup path's per-slice partial scores).
+size_t pq_ws_bytes(int64_t n_queries, int64_t nq, int64_t M, int64_t K, int64_t dsub,
+                   int64_t n_docs) {
+  size_t w = pq_lut_workspace_size(n_queries, nq, M, K, n_docs);
+  if (pq_mma_codebook_bytes(M, K, dsub)) {
+    const size_t m = pq_mma_workspace_size(n_queries, nq, M * dsub, n_docs);
+    if (m > w) w = m;
+  }
+  return w;
+}
+}  // namespace
+
+extern "C" size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, int64_t K,
+                                        int64_t dsub, int64_t n_docs) {
+  if (n_queries <= 0 || nq <= 0 || M <= 0 || K <= 0 || dsub <= 0 || n_docs < 0) return 0;
+  return pq_ws_bytes(n_queries, nq, M, K, dsub, n_docs);
 }
 
 extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
                              const void* codebook, int cb_dtype, int64_t M, int64_t K,
                              int64_t dsub, const uint8_t* codes, int64_t n_tokens,
                              const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
-                             float* out, void* workspace, size_t workspace_bytes, void* stream) {
+                             float* out, int mode, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (mode != TMS_PQ_FAST && mode != TMS_PQ_EXACT) return TMS_ERR_INVALID;
   if (n_queries < 0 || nq <= 0 || M <= 0 || K <= 0 || dsub <= 0 || n_docs < 0 || n_tokens < 0)
     return TMS_ERR_INVALID;
   if (q_dtype < TMS_F16 || q_dtype > TMS_F32 || cb_dtype < TMS_F16 || cb_dtype > TMS_F32)
@@ -230,11 +249,20 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   int status = TMS_OK;
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Tensor-core path: codes decoded through a shared-memory fp16 codebook into MMA operand tiles
+  // (fp16 queries, TMS_PQ_FAST); otherwise the exact fp32 table-lookup kernel below.
+  if (mode == TMS_PQ_FAST && q_dtype == TMS_F16 && pq_mma_codebook_bytes(M, K, dsub)) {
+    const int rc = pq_mma_maxsim(Q, n_queries, nq, codebook, cb_dtype, M, K, dsub, codes, n_tokens,
+                                 doc_offsets, n_docs, nd_uniform, out, workspace, workspace_bytes,
+                                 st);
+    if (rc != TMS_ERR_UNSUPPORTED) return rc;
+  }
   const int qs = pick_qs(M, K, nq);
   const size_t smem = static_cast<size_t>(M * K * qs) * 4;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
   const int nslice = static_cast<int>((nq + qs - 1) / qs);
-  const size_t need = tms_pq_workspace_size(n_queries, nq, M, K, n_docs);
+  const size_t need = pq_lut_workspace_size(n_queries, nq, M, K, n_docs);
   if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
   const bool m16 = (M == 16) && ((reinterpret_cast<uintptr_t>(codes) & 15) == 0);
 
@@ -261,7 +289,6 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   if (slices * parts > 0x7fffffffLL) return TMS_ERR_UNSUPPORTED;
   a.n_doc_parts = static_cast<int>(parts);
   const unsigned grid = static_cast<unsigned>(slices * parts);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
   switch (qs) {
     case 8: rc = launch_pq_t<8>(a, m16, grid, smem, st); break;

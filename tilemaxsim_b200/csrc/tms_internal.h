@@ -38,4 +38,13 @@ inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TMS_OK : TMS_E
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Tensor-core PQ path (dense kernel with decoder warps), defined in dense_maxsim.cu. Q is fp16.
+// pq_mma_codebook_bytes returns 0 when the shape does not fit that path.
+size_t pq_mma_codebook_bytes(int64_t M, int64_t K, int64_t dsub);
+size_t pq_mma_workspace_size(int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs);
+int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook, int cb_dtype,
+                  int64_t M, int64_t K, int64_t dsub, const uint8_t* codes, int64_t n_tokens,
+                  const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st);
+
 }  // namespace tms

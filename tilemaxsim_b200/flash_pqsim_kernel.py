@@ -5,7 +5,9 @@ methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_
 176-280). Scoring runs in the sm_100a ADC kernel (C ABI ``tms_pq_maxsim``): each CTA builds its
 query slice's distance table in shared memory and scores straight from the uint8 codes, so neither
 the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote both).
-``score_queries`` is the additive multi-query, ragged-corpus entry point.
+``score_queries`` is the additive multi-query, ragged-corpus entry point. By default fp16 queries
+run on the tensor cores: codes are decoded through a shared-memory fp16 codebook straight into the
+MMA operand tiles of the dense kernel (``exact=True`` keeps the table-lookup arithmetic).
 ``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
 """
 from __future__ import annotations
@@ -26,8 +28,14 @@ def _codes_u8(codes: torch.Tensor) -> torch.Tensor:
 class TileMaxSimPQ:
     """MaxSim over product-quantized documents (reference: src/flash_pqsim_kernel.py:176-280)."""
 
-    def __init__(self, codebook: torch.Tensor):
-        """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256."""
+    def __init__(self, codebook: torch.Tensor, exact: bool = False):
+        """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256.
+
+        exact=False (default): fp16 queries of a supported shape are scored on the tensor cores,
+        codes decoded in shared memory through the codebook rounded to fp16
+        (|error| <= 1e-3*|score| + 5e-3). exact=True: fp32 table lookups, the reference's
+        arithmetic (also used automatically for shapes the tensor path does not take)."""
+        self.exact = bool(exact)
         self.codebook = codebook.contiguous()
         self.M, self.K, self.dsub = codebook.shape
         self.d = self.M * self.dsub
@@ -72,14 +80,15 @@ class TileMaxSimPQ:
             out = torch.empty(Bq, n_docs, dtype=torch.float32, device=dev)
             if Bq == 0 or n_docs == 0:
                 return out
-            ws_bytes = lib.tms_pq_workspace_size(Bq, Nq, self.M, self.K, n_docs)
-            ws, ws_ptr = _lib.workspace(ws_bytes, dev, align=256)
+            ws_bytes = lib.tms_pq_workspace_size(Bq, Nq, self.M, self.K, self.dsub, n_docs)
+            ws, ws_ptr = _lib.workspace(ws_bytes, dev, align=1024)
             rc = lib.tms_pq_maxsim(
                 ctypes.c_void_p(Qb.data_ptr()), _lib.DTYPE_CODE[Qb.dtype], Bq, Nq,
                 ctypes.c_void_p(self.codebook.data_ptr()), _lib.DTYPE_CODE[self.codebook.dtype],
                 self.M, self.K, self.dsub, ctypes.c_void_p(codes_tokens.data_ptr()), codes_tokens.shape[0],
                 ctypes.c_void_p(offsets.data_ptr() if offsets is not None else 0), n_docs, nd,
-                ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws_ptr), ws_bytes,
+                ctypes.c_void_p(out.data_ptr()), _lib.TMS_PQ_EXACT if self.exact else _lib.TMS_PQ_FAST,
+                ctypes.c_void_p(ws_ptr), ws_bytes,
                 ctypes.c_void_p(_lib.stream_handle(dev)))
             _lib.check(rc, "tms_pq_maxsim")
             del ws
