@@ -101,9 +101,12 @@ class ClockSampler:
         if self._h is not None:
             self._t.join()
 
+    last_sm_mhz = None
+
     def summary(self) -> dict | None:
         if self._h is None or not self.samples:
             return None
+        ClockSampler.last_sm_mhz = statistics.median(self.samples)
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
                 "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
@@ -388,6 +391,7 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     ms, e2e_ms, dense_ms, T_total = t_all.tolist()
     if rank != 0:
         return
+    clocks = clk.summary()
 
     pairs = nqry * T_total
     value = pairs / (ms * 1e-3)
@@ -401,6 +405,11 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     else:
         ach = bytes_launch / (dense_ms * 1e-3) / 1e9
         peak, unit = pk["hbm_gbs"], "GB/s"
+    # The epilogue reads every fp32 similarity once from TMEM: B_q*Nq*T values per launch. TMEM ->
+    # register bandwidth measured at ~56 B/clk per SM (profiles/tmem_read_bandwidth.md).
+    tmem_bytes = 4.0 * nqry * nq * (T_total / world)
+    clk = ClockSampler.last_sm_mhz or 1965.0
+    tmem_peak = 56.0 * torch.cuda.get_device_properties(device).multi_processor_count * clk * 1e6 / 1e9
     traffic = None
     tf = ROOT / "profiles" / f"dense_maxsim_{args.config}_traffic.json"
     if tf.exists():
@@ -419,12 +428,16 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": ach, "peak": peak, "unit": unit,
                      "frac": ach / peak, "traffic": traffic,
                      "peak_src": f"{pk['src']} ({'bf16_tflops_sustained' if tensor_bound else 'hbm_gbs'})",
-                     "algorithmic": {"flops_per_launch": flops_launch, "bytes_per_launch": bytes_launch}},
+                     "algorithmic": {"flops_per_launch": flops_launch, "bytes_per_launch": bytes_launch},
+                     "tmem_read": {"achieved_gbs": tmem_bytes / (dense_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
+                                   "frac": tmem_bytes / (dense_ms * 1e-3) / 1e9 / tmem_peak,
+                                   "note": "epilogue reads B_q*Nq*T fp32 values from TMEM; peak = 56 B/clk/SM "
+                                           "measured (profiles/tmem_read_bandwidth.md) x SMs x median SM clock"}},
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s",
                 "h2d_bytes_per_step": Qh.numel() * Qh.element_size(),
                 "d2h_bytes_per_step": nqry * k * (4 + 8), "ms_per_step": e2e_ms},
         "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg)
