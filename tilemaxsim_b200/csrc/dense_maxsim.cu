@@ -99,7 +99,8 @@ __host__ __device__ inline SmemLayout dense_smem_layout(int TN, bool qres, int G
   L.carry_off = (L.bar_off + n_bars * 8u + 15u) & ~15u;
   L.x_off = L.carry_off + (split ? 0u : static_cast<uint32_t>(G) * kQTileRows * 4u);
   const uint32_t x_bytes =
-      split ? 2u * kEpiWarps * 32u * 4u + kEpiWarps * static_cast<uint32_t>(sizeof(PartMeta)) : 0u;
+      split ? 2u * (2u * kEpiWarps * 32u * 4u + kEpiWarps * static_cast<uint32_t>(sizeof(PartMeta)))
+            : 0u;  // split mode: two buffers (tile parity)
   L.cb_off = (L.x_off + x_bytes + 15u) & ~15u;
   L.misc_off = (L.cb_off + cb_bytes + 15u) & ~15u;
   L.total = L.misc_off + 64u;
@@ -467,13 +468,16 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
       // [32*ew, 32*ew+32) of every tile. Documents wholly inside a part are emitted by its warp;
       // the part's first (head) and last (tail) partial maxima go through shared memory and
       // warp 0 of the epilogue chains them across parts and tiles.
-      float* xhead = reinterpret_cast<float*>(smem + L.x_off);
-      float* xtail = xhead + kEpiWarps * 32;
-      PartMeta* xmeta = reinterpret_cast<PartMeta*>(xtail + kEpiWarps * 32);
+      // exchange area, double-buffered by tile parity: a warp writes tile t+2's buffer only
+      // after passing tile t+1's barrier, which the combine warp reaches after combining tile t
+      constexpr uint32_t kXBuf = 2u * kEpiWarps * 32u * 4u + kEpiWarps * sizeof(PartMeta);
       constexpr int kParts = TN / 32;
       float running = kNegInf;  // combine warp: max of the document open at the last part's end
       for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN, ++u) {
         const uint32_t slot = u % NSLOT;
+        float* xhead = reinterpret_cast<float*>(smem + L.x_off + (u & 1u) * kXBuf);
+        float* xtail = xhead + kEpiWarps * 32;
+        PartMeta* xmeta = reinterpret_cast<PartMeta*>(xtail + kEpiWarps * 32);
         const bool w_ok = wait_full(slot, u);
         tc_fence_after();
         const int ncol = (tok_hi - t0 < TN) ? static_cast<int>(tok_hi - t0) : TN;
@@ -555,11 +559,6 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
           doc = xmeta[n_parts - 1].end_doc;
           dend = xmeta[n_parts - 1].end_dend;
         }
-        // the exchange area is reused by the next tile only after the combine has read it
-        if (ew == 0)
-          asm volatile("bar.arrive 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
-        else
-          asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
       }
       if (ok && ew == 0 && !skip_math) {
         for (int64_t dd = doc; dd < doc_hi; ++dd) {
@@ -789,8 +788,18 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
   }
   if (p->stages < 1) p->stages = 1;
-  const SmemLayout L = dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages,
-                                        p->n_chunks_total == 1, p->cb_bytes);
+  const bool split = p->n_chunks_total == 1;
+  // the estimate above reserved a fixed allowance for barriers / carries / exchange area: move
+  // the stage count to what the exact layout allows (at most 4)
+  if (env_int("TMS_DENSE_STAGES", 0) == 0) {
+    while (p->stages > 1 && static_cast<int>(dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages,
+                                                               split, p->cb_bytes).total) > max_smem)
+      --p->stages;
+    while (p->stages < 4 && static_cast<int>(dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages + 1,
+                                                               split, p->cb_bytes).total) <= max_smem)
+      ++p->stages;
+  }
+  const SmemLayout L = dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages, split, p->cb_bytes);
   if (static_cast<int>(L.total) > max_smem) return TMS_ERR_UNSUPPORTED;
   // Token ranges per query group: the fewest that make groups x ranges a multiple of the SM count
   // (one balanced wave or several), but never fewer than fill one wave.
