@@ -26,7 +26,9 @@ def test_topk_ties_golden(cuda_device):
 
 
 @pytest.mark.parametrize("rows,n,k", [(3, 100_000, 1000), (64, 100_000, 1000), (2, 20_000, 10),
-                                      (1, 1_250_003, 100), (5, 16_385, 2048), (4, 7, 7)])
+                                      (1, 1_250_003, 100), (5, 16_385, 2048), (4, 7, 7),
+                                      (1, 400_000, 10), (1, 16_400, 1000), (300, 40_000, 5),
+                                      (1, 10_000_000, 1000)])
 def test_topk_random(rows, n, k, cuda_device):
     from tilemaxsim_b200 import topk
     g = torch.Generator().manual_seed(rows * n + k)

@@ -94,16 +94,32 @@ __global__ void __launch_bounds__(kTopkThreads)
 __global__ void __launch_bounds__(kTopkThreads)
     topk_select_kernel(const float* __restrict__ scores, int64_t n, int64_t ld, int k,
                        int64_t id_base, float* __restrict__ out_vals,
-                       int64_t* __restrict__ out_ids) {
+                       int64_t* __restrict__ out_ids, int64_t chunk, int n_chunks) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_prefix, s_mask, s_remaining;
   __shared__ uint32_t s_gt_pos, s_taken;
   __shared__ uint32_t warp_cnt[32];
   __shared__ int64_t cand_ids[kMaxK];
   __shared__ uint32_t cand_keys[kMaxK];
+  // Virtual row blockIdx.x = chunk c of row r: columns [c*chunk, c*chunk + chunk) of that row,
+  // whose own top-k (ids offset by c*chunk) lands in output row blockIdx.x; a row that is shorter
+  // than k is padded with (NaN, INT64_MAX), which ranks after everything.
   const int64_t row = blockIdx.x;
-  const float* s = scores + row * ld;
+  const int64_t r = row / n_chunks, c = row - r * n_chunks;
+  const float* s = scores + r * ld + c * chunk;
+  const int64_t n_all = n;
+  n = (n_all - c * chunk < chunk) ? n_all - c * chunk : chunk;
+  id_base += c * chunk;
+  const int k_out = k;
+  if (k > n) k = static_cast<int>(n);
   const int tid = threadIdx.x;
+  if (n <= 0) {  // empty slice: padding only
+    for (int i = tid; i < k_out; i += blockDim.x) {
+      out_vals[row * k_out + i] = key2f(0u);
+      out_ids[row * k_out + i] = INT64_MAX;
+    }
+    return;
+  }
   const int lane = tid & 31, wid = tid >> 5;
 
   if (tid == 0) {
@@ -190,9 +206,9 @@ __global__ void __launch_bounds__(kTopkThreads)
   }
   __syncthreads();
   bitonic_sort(cand_keys, cand_ids, P);
-  for (int i = tid; i < k; i += blockDim.x) {
-    out_vals[row * k + i] = key2f(cand_keys[i]);
-    out_ids[row * k + i] = cand_ids[i] + id_base;
+  for (int i = tid; i < k_out; i += blockDim.x) {
+    out_vals[row * k_out + i] = i < k ? key2f(cand_keys[i]) : key2f(0u);
+    out_ids[row * k_out + i] = i < k ? cand_ids[i] + id_base : INT64_MAX;
   }
 }
 
@@ -201,18 +217,28 @@ __global__ void __launch_bounds__(kTopkThreads)
 
 using namespace tms;
 
+namespace {
+// Long rows with few of them: split each row into n_chunks slices selected by separate CTAs, then
+// sort-merge the n_chunks * k candidates per row. Depends on the shape only.
+int topk_chunks(int64_t rows, int64_t n, int64_t k) {
+  if (n <= kSortMax || rows <= 0 || k <= 0) return 1;
+  int64_t c = (n + 16383) / 16384;      // slices of at least ~16k scores
+  const int64_t by_merge = kSortMax / k;  // the merge sorts at most kSortMax candidates
+  const int64_t by_grid = rows >= 296 ? 1 : 296 / rows;
+  if (c > by_merge) c = by_merge;
+  if (c > by_grid) c = by_grid;
+  return c < 2 ? 1 : static_cast<int>(c);
+}
+}  // namespace
+
 extern "C" size_t tms_topk_workspace_size(int64_t rows, int64_t n, int64_t k) {
-  (void)rows;
-  (void)n;
-  (void)k;
-  return 0;
+  const int c = topk_chunks(rows, n, k);
+  return c > 1 ? static_cast<size_t>(rows * c * k) * 12 + 256 : 0;
 }
 
 extern "C" int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, int64_t k,
                         const int64_t* ids_in, int64_t ld_ids, int64_t id_base, float* out_vals,
                         int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (rows < 0 || n < 0 || k < 0 || ld < n) return TMS_ERR_INVALID;
   if (rows == 0 || k == 0) return TMS_OK;
   if (k > n || !scores || !out_vals || !out_ids) return TMS_ERR_INVALID;
@@ -234,7 +260,29 @@ extern "C" int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld
     return cuda_status(cudaGetLastError());
   }
   if (ids_in) return TMS_ERR_UNSUPPORTED;  // explicit ids are for shard merges (short rows)
+  const int c = topk_chunks(rows, n, k);
+  if (c > 1 && workspace && workspace_bytes >= tms_topk_workspace_size(rows, n, k) &&
+      rows * c <= 0x7fffffffLL) {
+    // slice top-k into the workspace, then one sort-merge per row (ids carried explicitly)
+    int64_t* cand_ids = reinterpret_cast<int64_t*>(
+        (reinterpret_cast<uintptr_t>(workspace) + 15) & ~static_cast<uintptr_t>(15));
+    float* cand_vals = reinterpret_cast<float*>(cand_ids + rows * c * k);
+    const int64_t chunk = (n + c - 1) / c;
+    topk_select_kernel<<<static_cast<unsigned>(rows * c), kTopkThreads, 0, st>>>(
+        scores, n, ld, static_cast<int>(k), id_base, cand_vals, cand_ids, chunk, c);
+    if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
+    const int64_t m = static_cast<int64_t>(c) * k;
+    int P = 1;
+    while (P < m) P <<= 1;
+    const size_t smem = static_cast<size_t>(P) * 12;
+    if (cudaFuncSetAttribute(topk_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return TMS_ERR_CUDA;
+    topk_sort_kernel<<<static_cast<unsigned>(rows), kTopkThreads, smem, st>>>(
+        cand_vals, m, m, static_cast<int>(k), cand_ids, m, 0, out_vals, out_ids);
+    return cuda_status(cudaGetLastError());
+  }
   topk_select_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, st>>>(
-      scores, n, ld, static_cast<int>(k), id_base, out_vals, out_ids);
+      scores, n, ld, static_cast<int>(k), id_base, out_vals, out_ids, n, 1);
   return cuda_status(cudaGetLastError());
 }
