@@ -155,7 +155,9 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const bool split = a.n_chunks_total == 1;  // one query: column-split epilogue
+  // one query tile (1-4 chunks): column-split epilogue over nc = 1, 2 or 4 replicated chunks
+  const bool split = a.n_mtiles == 1;
+  const int split_nc = a.n_chunks_total == 1 ? 1 : a.n_chunks_total == 2 ? 2 : 4;
   const SmemLayout L = dense_smem_layout(TN, QRES, a.G, a.kc, a.stages, split, a.cb_bytes);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t q_s = sbase + L.q_off;
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     int64_t dend = doc_end(doc);
     uint32_t u = 0;
     bool ok = true;
-    if (split) {
+    if (split && split_nc == 1) {
       // ---- split mode: one query replicated in all four lane quarters; warp ew owns columns
       // [32*ew, 32*ew+32) of every tile. Documents wholly inside a part are emitted by its warp;
       // the part's first (head) and last (tail) partial maxima go through shared memory and
@@ -563,6 +565,164 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
       if (ok && ew == 0 && !skip_math) {
         for (int64_t dd = doc; dd < doc_hi; ++dd) {
           emit(0, dd, running);
+          running = kNegInf;
+        }
+      }
+    } else if (split) {
+      // ---- column-split mode (one query tile holding nc = 1, 2 or 4 chunks): the pack kernel
+      // replicates the chunks over the four lane quarters (quarter lq holds chunk lq % nc), so
+      // W = 8 / nc warps can read each chunk; warp ew (lane quarter lg = (ew + 2) & 3) takes part
+      // p = ew / nc, columns [p*PC, p*PC + PC) of every tile of chunk c = lg % nc. The owner of
+      // part p of chunk c is warp ew = p*nc + ((c - 2) & (nc - 1)). Documents wholly inside a part are
+      // emitted by its warp; the part's head (max up to its first document end) and tail (max
+      // after its last) go through shared memory, and the chunk's part-0 warp chains them across
+      // parts and tiles.
+      // exchange area, double-buffered by tile parity: a warp writes tile t+2's buffer only
+      // after passing tile t+1's barrier, which the combine warps reach after combining tile t
+      constexpr uint32_t kXBuf = 2u * kEpiWarps * 32u * 4u + kEpiWarps * sizeof(PartMeta);
+      const int nc = split_nc;
+      const int c = lg % nc;  // this warp's lane quarter holds chunk c
+      const int pw = ew / nc;
+      const int W = (8 / nc < TN / 32) ? 8 / nc : TN / 32;  // parts per chunk (>= 32 columns)
+      const int PC = TN / W;
+      const bool chunk_ok = c < a.n_chunks_total;
+      float running = kNegInf;  // combine warp: max of the chunk's document open at the tile end
+      for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN, ++u) {
+        const uint32_t slot = u % NSLOT;
+        float* xhead = reinterpret_cast<float*>(smem + L.x_off + (u & 1u) * kXBuf);
+        float* xtail = xhead + kEpiWarps * 32;
+        PartMeta* xmeta = reinterpret_cast<PartMeta*>(xtail + kEpiWarps * 32);
+        const bool w_ok = wait_full(slot, u);
+        tc_fence_after();
+        const int ncol = (tok_hi - t0 < TN) ? static_cast<int>(tok_hi - t0) : TN;
+        const int pc0 = pw * PC;
+        float head = kNegInf, tail = kNegInf;
+        int has_b = 0;
+        int64_t head_doc = -1, dd = doc, de = dend;
+        if (w_ok && chunk_ok && pw < W && pc0 < ncol && !skip_math) {
+          auto rel = [&](int64_t e) -> int {
+            const int64_t x = e - t0;
+            return x > 4 * TN ? 4 * TN : static_cast<int>(x);
+          };
+          int dcol = rel(de);
+          while (dcol < pc0) {  // documents that end before this part belong to earlier parts
+            ++dd;
+            de = doc_end(dd);
+            dcol = rel(de);
+          }
+          const int pend = (ncol < pc0 + PC) ? ncol : pc0 + PC;
+          float rm = kNegInf;
+          auto reduce32 = [&](const uint32_t(&v)[32], int cb) {
+            if (dcol >= cb + 32 && pend >= cb + 32) {
+              rm = max32(rm, v);  // the whole block lies in the open document
+            } else {
+              const int n = (pend - cb < 32) ? pend - cb : 32;
+              int lo = 0;
+              while (true) {
+                const int hi = (dcol - cb < n) ? dcol - cb : n;
+                rm = range_max32(rm, v, lo, hi);
+                if (dcol - cb >= n) break;
+                if (!has_b) {
+                  head = rm;
+                  head_doc = dd;
+                  has_b = 1;
+                } else {
+                  emit(c, dd, rm);
+                }
+                rm = kNegInf;
+                ++dd;
+                de = doc_end(dd);
+                dcol = rel(de);
+                lo = hi;
+              }
+            }
+          };
+          const uint32_t tbase = t_lane + slot * TN + pc0;
+          if (PC == 32) {
+            // one 32-column block per part (single query): one load, straight-line reduction
+            uint32_t r[32];
+            tmem_ld32_async(tbase, r);
+            tmem_wait_ld32(r);
+            const int n = pend - pc0;
+            int lo = 0;
+            while (true) {
+              const int hi = (dcol - pc0 < n) ? dcol - pc0 : n;
+              rm = (lo == 0 && hi == 32) ? max32(rm, r) : range_max32(rm, r, lo, hi);
+              if (dcol - pc0 >= n) break;
+              if (!has_b) {
+                head = rm;
+                head_doc = dd;
+                has_b = 1;
+              } else {
+                emit(c, dd, rm);
+              }
+              rm = kNegInf;
+              ++dd;
+              de = doc_end(dd);
+              dcol = rel(de);
+              lo = hi;
+            }
+          } else {
+          // 32-column TMEM loads, double-buffered (block b+1 in flight while b is reduced)
+          uint32_t ra[32], rb[32];
+          tmem_ld32_async(tbase, ra);
+#pragma unroll
+          for (int bk = 0; bk < 4; ++bk) {
+            uint32_t(&cur)[32] = (bk & 1) ? rb : ra;
+            uint32_t(&nxt)[32] = (bk & 1) ? ra : rb;
+            const int cb = pc0 + 32 * bk;
+            if (32 * bk < PC && cb < pend) {
+              tmem_wait_ld32(cur);
+              if (32 * (bk + 1) < PC && cb + 32 < pend) tmem_ld32_async(tbase + 32 * (bk + 1), nxt);
+              reduce32(cur, cb);
+            }
+          }
+          }
+          if (has_b) tail = rm; else head = rm;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar(slot));  // this warp is done with the TMEM slot
+        xhead[ew * 32 + lane] = head;
+        xtail[ew * 32 + lane] = tail;
+        if (lane == 0) {
+          xmeta[ew].head_doc = head_doc;
+          xmeta[ew].has_b = has_b;
+          xmeta[ew].end_doc = dd;
+          xmeta[ew].end_dend = de;
+        }
+        // all eight warps agree on whether every wait succeeded before anyone waits again
+        uint32_t all_ok;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.and.pred q, 1, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}\n"
+            : "=r"(all_ok)
+            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32)
+            : "memory");
+        if (!(ok = all_ok != 0)) break;
+        const int n_parts = (ncol + PC - 1) / PC;
+        if (!skip_math) {
+          if (pw == 0 && chunk_ok) {
+            for (int pp = 0; pp < n_parts; ++pp) {
+              const int xe = nc * pp + ((c - 2) & (nc - 1));  // the warp owning part pp of chunk c
+              running = fmaxf(running, xhead[xe * 32 + lane]);
+              if (xmeta[xe].has_b) {
+                emit(c, xmeta[xe].head_doc, running);
+                running = xtail[xe * 32 + lane];
+              }
+            }
+          }
+          // the document walk is the same for every chunk: take it from chunk 0's last part
+          const int xl = nc * (n_parts - 1) + ((0 - 2) & (nc - 1));
+          doc = xmeta[xl].end_doc;
+          dend = xmeta[xl].end_dend;
+        }
+      }
+      if (ok && pw == 0 && chunk_ok && !skip_math) {
+        for (int64_t dd = doc; dd < doc_hi; ++dd) {
+          emit(c, dd, running);
           running = kNegInf;
         }
       }
@@ -680,7 +840,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
 
 // Packs Q (n_queries, nq, d) into 128-row M tiles: chunk c (32 rows) = rows [32p, 32p+32) of query
 // c / nchunk (p = c % nchunk); rows past nq and chunks past the last query are zero. With
-// `replicate` (a single chunk) the chunk fills all four 32-row quarters of the tile.
+// `replicate` (one query tile of 1 or 2 chunks) quarter q of the tile holds chunk q % n_chunks.
 __global__ void pack_query_tiles_kernel(const uint4* __restrict__ q, uint4* __restrict__ qp,
                                         int64_t n_vec_total, int vec_per_row, int nq, int nchunk,
                                         int n_chunks_total, int replicate) {
@@ -688,7 +848,8 @@ __global__ void pack_query_tiles_kernel(const uint4* __restrict__ q, uint4* __re
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / vec_per_row;
     const int v = static_cast<int>(i - r * vec_per_row);
-    const int64_t c = replicate ? 0 : (r >> 5);  // replicate: the single chunk in all 4 quarters
+    // replicate: 1 or 2 chunks repeated over the tile's four 32-row quarters
+    const int64_t c = replicate ? (r >> 5) % n_chunks_total : (r >> 5);
     const int ln = static_cast<int>(r & 31);
     uint4 val = make_uint4(0, 0, 0, 0);
     if (c < n_chunks_total) {
@@ -788,7 +949,7 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
   }
   if (p->stages < 1) p->stages = 1;
-  const bool split = p->n_chunks_total == 1;
+  const bool split = p->n_mtiles == 1;
   // the estimate above reserved a fixed allowance for barriers / carries / exchange area: move
   // the stage count to what the exact layout allows (at most 4)
   if (env_int("TMS_DENSE_STAGES", 0) == 0) {
@@ -821,7 +982,7 @@ template <int TN, bool QRES, bool TF32, bool PQ = false>
 int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
                    const DensePlan& p, cudaStream_t st) {
   auto kern = dense_maxsim_kernel<TN, QRES, TF32, PQ>;
-  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_chunks_total == 1,
+  const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_mtiles == 1,
                                          p.cb_bytes);
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
@@ -908,7 +1069,7 @@ extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int
     pack_query_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(Q),
                                                     reinterpret_cast<uint4*>(qp), n_vec, vpr,
                                                     static_cast<int>(nq), p.nchunk,
-                                                    p.n_chunks_total, p.n_chunks_total == 1);
+                                                    p.n_chunks_total, p.n_mtiles == 1 && p.n_chunks_total <= 2);
     if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
   }
 
@@ -974,7 +1135,7 @@ extern "C" int tms_dense_plan_info(int dtype, int64_t n_queries, int64_t nq, int
   info[5] = p.n_ranges;
   info[6] = p.n_mtiles;
   info[7] = p.kc;
-  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_chunks_total == 1, 0).total;
+  info[8] = dense_smem_layout(p.TN, p.qres, p.G, p.kc, p.stages, p.n_mtiles == 1, 0).total;
   info[9] = static_cast<int64_t>(p.n_ranges) * p.n_groups;
   return TMS_OK;
 }
@@ -1024,7 +1185,7 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
   pack_query_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(Q),
                                                   reinterpret_cast<uint4*>(qp), n_vec, vpr,
                                                   static_cast<int>(nq), p.nchunk, p.n_chunks_total,
-                                                  p.n_chunks_total == 1);
+                                                  p.n_mtiles == 1 && p.n_chunks_total <= 2);
   if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
   CUtensorMap qm;
   rc = encode_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qp, static_cast<uint64_t>(d),
