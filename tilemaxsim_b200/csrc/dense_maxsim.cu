@@ -15,11 +15,15 @@
 //  * Doc tokens are streamed as TN-token tiles (TN = 256 or 128) by TMA (128-byte swizzle) into a
 //    ring of shared-memory stages; each D byte is read from HBM once per CTA group.
 //  * One thread issues tcgen05.mma (kind::f16 for fp16/bf16, kind::tf32 for fp32 inputs) into a
-//    double-buffered fp32 accumulator in TMEM (2 x TN columns).
-//  * Four epilogue warps read their 32 lanes with tcgen05.ld and run a segmented max along the
-//    columns (doc boundaries are warp-uniform, taken from the offsets array), then one warp-shuffle
-//    sum over the 32 query-token lanes per finished document. The Nq x Nd similarity matrix never
-//    leaves the SM.
+//    ring of fp32 accumulators in TMEM (512 / TN slots of TN columns).
+//  * Epilogue warps read their 32 lanes with tcgen05.ld and run a segmented max along the columns
+//    (doc boundaries are warp-uniform, taken from the offsets array), then one warp-shuffle sum over
+//    the 32 query-token lanes per finished document. The Nq x Nd similarity matrix never leaves the
+//    SM. Rows mode (several query tiles): two groups of four warps take alternate query tiles.
+//    Column-split mode (one query tile): the chunks are replicated over the lane quarters and all
+//    eight warps share each tile's columns, chaining partial maxima through shared memory.
+//  * The epilogue reads every fp32 similarity once from TMEM, and tcgen05.ld sustains ~56 B/clk per
+//    SM: for large query batches that, not the tensor pipe, bounds the kernel.
 //  * The CTA grid is (token range) x (query group). Token ranges are cut at document boundaries
 //    (warp-cooperative binary search on the offsets), so no document straddles two CTAs and no
 //    cross-CTA merge or atomic is needed: results are deterministic.
