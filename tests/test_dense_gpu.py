@@ -169,21 +169,35 @@ def test_full_size_rerank_consistency(cuda_device):
     close(sub, O.maxsim_ragged(Qb.cpu(), Dsub.cpu(), sub_off))
 
 
-def test_bounded_wait_reports_timeout(cuda_device):
+@pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor"])
+def test_bounded_wait_reports_timeout(case, cuda_device):
     """Fault knob: the producer issues no load, so every consumer wait runs out after the (short)
     limit; the kernel returns, the host reads TMS_ERR_TIMEOUT, and the context stays usable."""
-    from tilemaxsim_b200 import _lib, maxsim_batched
+    from tilemaxsim_b200 import TileMaxSimPQ, _lib, maxsim_batched
     lib = _lib.load()
-    c = R.ragged_case(n_queries=1, n_docs=20, seed=3)
-    args = [c["Qb"].to(cuda_device), c["D"].to(cuda_device), c["offsets"].to(cuda_device)]
+    if case == "pq_tensor":
+        cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
+        pq = TileMaxSimPQ(cb)
+        codes = torch.randint(0, 256, (40 * 64, 16), generator=R.gen(4), dtype=torch.uint8).to(cuda_device)
+        off = (torch.arange(41, dtype=torch.int64) * 64).to(cuda_device)
+        Qb = R.normalized((5, 32, 128), 5).to(cuda_device)
+        run = lambda: pq.score_queries(Qb, codes, off)  # noqa: E731
+        want = O.pq_maxsim_adc_ragged(Qb.cpu(), cb.cpu(), codes.cpu(), off.cpu().numpy())
+        tol = (1e-3, 5e-3)
+    else:
+        c = R.ragged_case(n_queries=1 if case == "single_query" else 9, n_docs=20, seed=3)
+        args = [c["Qb"].to(cuda_device), c["D"].to(cuda_device), c["offsets"].to(cuda_device)]
+        run = lambda: maxsim_batched(*args)  # noqa: E731
+        want = O.maxsim_ragged(c["Qb"], c["D"], c["offsets"].numpy())
+        tol = (RTOL, ATOL)
     assert _lib.last_device_error(cuda_device)[0] == _lib.TMS_OK
-    lib.tms_set_debug(50_000_000, 1)  # 50 ms limit, producer silent
+    lib.tms_set_debug(50_000_000, 1)  # 50 ms limit, producer / decoders silent
     try:
-        maxsim_batched(*args)
+        run()
         rc, word = _lib.last_device_error(cuda_device)
     finally:
         lib.tms_set_debug(2_000_000_000, 0)
     assert rc == _lib.TMS_ERR_TIMEOUT and word & 0x80000000
     # the context still works and the error word was cleared
-    close(maxsim_batched(*args), O.maxsim_ragged(c["Qb"], c["D"], c["offsets"].numpy()))
+    close(run(), want, *tol)
     assert _lib.last_device_error(cuda_device)[0] == _lib.TMS_OK

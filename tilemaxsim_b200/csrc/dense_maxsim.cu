@@ -1220,7 +1220,7 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
   args.pq_K = static_cast<int>(K);
   args.pq_dsub = static_cast<int>(dsub);
   args.cb_bytes = static_cast<uint32_t>(cb_bytes);
-  args.debug_flags = debug_flags() & 1;
+  args.debug_flags = debug_flags();
   rc = (p.TN == 256) ? launch_dense_t<256, true, false, true>(qm, qm, args, p, st)
                      : launch_dense_t<128, true, false, true>(qm, qm, args, p, st);
   if (rc != TMS_OK || p.nchunk == 1) return rc;
