@@ -1,0 +1,55 @@
+"""Host-side checks of the drop-in Python API (no GPU): argument validation happens before any
+kernel call, and CPU tensors are rejected loudly (there is no CPU fallback)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+
+def test_cpu_tensors_are_rejected():
+    from tilemaxsim_b200 import flash_maxsim_v2_multiquery, maxsim_batched, topk
+    Q = torch.zeros(32, 128, dtype=torch.float16)
+    D = torch.zeros(4, 10, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        flash_maxsim_v2_multiquery(Q, D)
+    with pytest.raises(ValueError, match="CUDA"):
+        maxsim_batched(Q, D.view(40, 128), torch.tensor([0, 10, 40]))
+    with pytest.raises(ValueError, match="CUDA"):
+        topk(torch.zeros(3, 50), 5)
+
+
+def test_shape_errors_match_the_reference():
+    from tilemaxsim_b200 import flash_maxsim_batch, flash_maxsim_single, flash_maxsim_v2
+    Q = torch.zeros(32, 128, dtype=torch.float16)
+    with pytest.raises(AssertionError):  # src/flash_maxsim_kernel.py:180
+        flash_maxsim_single(Q, torch.zeros(10, 64, dtype=torch.float16))
+    with pytest.raises(AssertionError):  # src/flash_maxsim_kernel.py:213
+        flash_maxsim_batch(Q, torch.zeros(2, 10, 64, dtype=torch.float16))
+    with pytest.raises(ValueError):
+        flash_maxsim_v2(Q, torch.zeros(10, 128, dtype=torch.float16))
+
+
+def test_pq_shape_errors():
+    from tilemaxsim_b200 import TileMaxSimPQ
+    pq = TileMaxSimPQ(torch.zeros(16, 256, 8))
+    assert (pq.M, pq.K, pq.dsub, pq.d) == (16, 256, 8, 128)
+    with pytest.raises(AssertionError):  # src/flash_pqsim_kernel.py:226
+        pq.score_batch(torch.zeros(32, 128, dtype=torch.float16), torch.zeros(2, 10, 8, dtype=torch.uint8))
+    with pytest.raises(AssertionError):  # src/flash_pqsim_kernel.py:201
+        pq.build_distance_table(torch.zeros(32, 64))
+
+
+def test_reference_baselines_run_on_cpu():
+    """pytorch_maxsim_naive / _loop / pytorch_pqsim_baseline are the reference's plain-torch
+    baselines, kept in the drop-in modules; they agree with the oracle on CPU."""
+    import numpy as np
+    import recipes as R
+    from oracle import maxsim_oracle as O
+    from tilemaxsim_b200 import pytorch_maxsim_loop, pytorch_maxsim_naive, pytorch_pqsim_baseline
+    c = R.v1_selfcheck_case()
+    want = O.maxsim_padded(c["Q"], c["D"])
+    np.testing.assert_allclose(pytorch_maxsim_naive(c["Q"], c["D"]).numpy(), want, rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(pytorch_maxsim_loop(c["Q"], c["D"]).numpy(), want, rtol=1e-5, atol=1e-4)
+    p = R.pq_case()
+    np.testing.assert_allclose(pytorch_pqsim_baseline(p["Q"], p["codebook"], p["codes"]).numpy(),
+                               O.pq_maxsim_decompress(p["Q"], p["codebook"], p["codes"]), rtol=1e-5, atol=1e-4)
