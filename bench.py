@@ -243,6 +243,8 @@ PQ_CONFIGS = {
     # name: (n_queries, nq, M, K, dsub, n_docs per GPU, nd, k)
     "c4": (16, 32, 16, 256, 8, 1_000_000, 128, 100),
     "c4_small": (16, 32, 16, 256, 8, 50_000, 128, 100),
+    # single-query PQ over the same corpus (the north star's single-query PQ path)
+    "q1_pq": (1, 32, 16, 256, 8, 1_000_000, 128, 100),
 }
 
 

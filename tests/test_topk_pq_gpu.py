@@ -96,6 +96,54 @@ def test_pq_ragged_multiquery(M, K, dsub, nq, path, cuda_device):
     np.testing.assert_allclose(got[~inf], want[~inf], rtol=rtol, atol=atol)
 
 
+@pytest.mark.parametrize("nqry,M,K,dsub,nq,lengths", [
+    (1, 16, 256, 8, 32, "ragged"), (2, 16, 256, 8, 32, "ragged"), (4, 16, 256, 8, 32, "ragged"),
+    (3, 16, 256, 8, 20, "ragged"), (1, 16, 256, 8, 64, "ragged"), (2, 32, 256, 8, 40, "ragged"),
+    (1, 32, 256, 8, 32, "ragged"), (1, 8, 256, 8, 32, "ragged"), (2, 8, 256, 8, 30, "tiny"),
+    (1, 8, 256, 16, 32, "ragged"), (1, 16, 100, 8, 5, "ragged"), (1, 16, 256, 8, 32, "tiny"),
+    (2, 16, 256, 8, 32, "one_long")])
+def test_pq_small_batch_token_rows(nqry, M, K, dsub, nq, lengths, cuda_device):
+    """Small query batches (1-2 chunks of 32 query rows) take the token-rows tensor kernel: decoded
+    tokens in TMEM as the MMA's A operand, per-lane running maxima, a transposing max per finished
+    document (3-4 chunks check the decoder-warp kernel on the same cases). Ragged
+    corpora with empty documents, documents of 1-3 tokens (several boundaries per window), and one
+    document longer than a CTA's share of the corpus."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    if lengths == "ragged":
+        lens = R.ragged_lengths(700, 0, 300, seed=nqry + M)
+    elif lengths == "tiny":
+        lens = R.ragged_lengths(3000, 0, 3, seed=7)
+    else:
+        lens = R.ragged_lengths(300, 0, 40, seed=8)
+        lens[100] = 20_000
+    off = R.offsets_from_lengths(lens)
+    cb = R.randn((M, K, dsub), 3, torch.float32)
+    Qb = R.normalized((nqry, nq, M * dsub), 4)
+    codes = torch.randint(0, K, (int(off[-1]), M), generator=R.gen(5), dtype=torch.uint8)
+    pq = TileMaxSimPQ(cb.to(cuda_device))
+    got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device),
+                           torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=5e-3)
+
+
+def test_pq_single_query_full_size_property(cuda_device):
+    """Single query over a 400k-document slice of BASELINE config 4 (51.2M code rows) on the
+    token-rows kernel agrees with the exact table-lookup path on every score."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    g = torch.Generator(device=cuda_device).manual_seed(6)
+    n, nd = 400_000, 128
+    codes = torch.randint(0, 256, (n * nd, 16), generator=g, device=cuda_device, dtype=torch.uint8)
+    off = torch.arange(n + 1, device=cuda_device, dtype=torch.int64) * nd
+    cb = torch.randn(16, 256, 8, generator=g, device=cuda_device)
+    Q = torch.nn.functional.normalize(torch.randn(1, 32, 128, generator=g, device=cuda_device), dim=-1).half()
+    fast = TileMaxSimPQ(cb).score_queries(Q, codes, off)
+    exact = TileMaxSimPQ(cb, exact=True).score_queries(Q, codes, off)
+    torch.testing.assert_close(fast, exact, rtol=1e-3, atol=5e-3)
+
+
 def test_pq_tensor_path_full_size_property(cuda_device):
     """BASELINE config 4 shape on a 200k-document slice (25.6M code rows): the tensor-core path
     agrees with the exact table-lookup path on every score (1e-3 relative + 5e-3)."""

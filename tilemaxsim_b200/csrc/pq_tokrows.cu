@@ -1,0 +1,492 @@
+// pq_tokrows.cu -- PQ-ADC on the sm_100a tensor cores for small query batches (one or two
+// 32-row query chunks), with the document tokens on the TMEM lanes.
+//
+//   score[q, doc] = sum_i max_{j in doc} sum_m <Q[q,i,m*dsub:(m+1)*dsub], C[m, codes[j,m], :]>
+//
+// Reference semantics: src/flash_pqsim_kernel.py:190-211 (distance table T[i,m,k] = <q_i,m, c_m,k>)
+// and :213-280 (TileMaxSimPQ.score_batch: per token the sum over subspaces of T[i,m,code_m], max
+// over the document's tokens, sum over the query tokens). The sum over m of <q_i,m, c_m,code_m>
+// is <q_i, decode(codes_j)>, the dot product with the token's reconstructed vector, so the kernel
+// rebuilds each token from the codebook and lets the tensor cores take the dot products.
+//
+// Design (the single-query PQ hot path):
+//  * Decoded tokens are the MMA's A operand: M = 128 token rows x K = d, written from registers
+//    straight into TMEM with tcgen05.st (lane = token, 32-bit column c = fp16 elements 2c, 2c+1).
+//    No shared-memory store and no replicated query tile: the only shared-memory traffic per token
+//    is the codebook gather (M random 16-byte reads at dsub = 8), which bounds the kernel.
+//  * The query rows are the B operand (N = 32 or 64), resident in shared memory in the 128-byte-
+//    swizzle K-major layout. S^T = Dtile . Q^T lands with one token per TMEM lane and one query row
+//    per column.
+//  * The CTA's token range (cut at document boundaries) is cut again into four document-aligned
+//    sub-ranges, one per TMEM lane quarter: lane 32q + l of tile j holds token sub_tok[q] + 32j + l.
+//    Every epilogue warp therefore walks one contiguous token stream and owns whole documents:
+//    no cross-warp merge, deterministic results.
+//  * Epilogue: lane l keeps the running max over its tokens of the open document for every query
+//    row (elementwise, no shuffles); when the document ends, a transposing max (31 shuffles)
+//    leaves row l's maximum in lane l and a warp sum over the query rows gives the score.
+//  * A hand-off through an mbarrier costs ~500 cycles on this part, so TMEM holds as many tiles
+//    in flight as fit (5 at N = 32: 64 decoded-token columns + 32 accumulator columns each).
+//
+// Warp roles (512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 = decoders (lane
+// quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column blocks of every
+// tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only help in the prologue.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "tms_device.cuh"
+#include "tms_internal.h"
+
+namespace tms {
+
+namespace {
+
+constexpr int kTrThreads = 512;
+constexpr int kTrDecWarp0 = 4;
+constexpr int kTrEpiWarp0 = 12;
+constexpr int kTrMaxChunks = 2;  // N = 32 x chunks <= 64 query rows per CTA
+constexpr float kTrNegInf = -__builtin_huge_valf();
+
+struct TrArgs {
+  DocLayout docs;
+  const uint8_t* codes;
+  const __half* Q;  // (n_queries, nq, d) fp16
+  const void* codebook;
+  float* out;  // (n_chunks, n_docs): final scores when nchunk == 1, else per-chunk partials
+  uint32_t* err;
+  uint64_t timeout_ns;
+  int cb_dtype, M, K, dsub, d;
+  int nq, nchunk, n_chunks;  // query rows per query, 32-row chunks per query, chunks in total
+  int nslot;                 // TMEM slots (A columns + accumulator columns each)
+  int n_ranges;
+  int debug_flags;  // bit 0: decoders write nothing (exercises the bounded waits)
+};
+
+struct TrLayout {
+  uint32_t b_off, cb_off, bar_off, misc_off, total;
+};
+__host__ __device__ inline TrLayout tr_layout(int N, int d, uint32_t cb_bytes, int nslot) {
+  TrLayout L;
+  L.b_off = 0;
+  L.cb_off = static_cast<uint32_t>((d / 64) * N * 128);
+  L.bar_off = (L.cb_off + cb_bytes + 15u) & ~15u;
+  L.misc_off = L.bar_off + static_cast<uint32_t>(3 * nslot + 1) * 8u;
+  L.total = L.misc_off + 128u;
+  return L;
+}
+struct TrMisc {
+  uint32_t tmem;
+  int abort;
+  int never;  // stays 0: the final drain wait is bounded by time only
+  int n_tiles;
+  int64_t sub_doc[5];
+  int64_t sub_tok[5];
+};
+
+// Lane l receives max over the 32 lanes of v[l]; destroys v. 31 shuffles: at each step a lane
+// keeps the half of its values whose row index has its own lane bit and trades the other half.
+__device__ __forceinline__ float xpose_max32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? v[i] : v[i + w];
+      const float keep = up ? v[i + w] : v[i];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
+    }
+  }
+  return v[0];
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int N = NCH * 32;
+  const int acols = a.d / 2;  // TMEM columns of one decoded tile (fp16 pairs)
+  const int S = a.nslot;
+  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(a.M * a.K * a.dsub * 2), S);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t b_s = sbase + L.b_off;
+  const uint32_t bar_s = sbase + L.bar_off;
+  auto afull_bar = [&](int s) { return bar_s + 8u * s; };
+  auto accf_bar = [&](int s) { return bar_s + 8u * (S + s); };
+  auto free_bar = [&](int s) { return bar_s + 8u * (2 * S + s); };
+  const uint32_t done_bar = bar_s + 8u * (3 * S);
+  TrMisc* misc = reinterpret_cast<TrMisc*>(smem + L.misc_off);
+  volatile int* abort_flag = &misc->abort;
+  __half* cbs = reinterpret_cast<__half*>(smem + L.cb_off);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const DocLayout docs = a.docs;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(afull_bar(s), 8);  // the two decoder warps of each lane quarter
+      mbar_init(accf_bar(s), 1);
+      mbar_init(free_bar(s), 4);   // the four epilogue warps
+    }
+    mbar_init(done_bar, 1);
+    misc->abort = (sbase & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
+    misc->never = 0;
+    if (misc->abort) atomicCAS(a.err, 0u, kDevErrTimeout | 31u);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    // This CTA's document-aligned token range, and its four document-aligned quarters.
+    const int range = blockIdx.x;
+    const int64_t t_first = docs.start(0);
+    const int64_t span = docs.start(docs.n_docs) - t_first;
+    const int64_t doc_lo = (range == 0) ? 0 : warp_lower_bound(docs, t_first + span * range / a.n_ranges);
+    int64_t doc_hi = (range == a.n_ranges - 1)
+                         ? docs.n_docs
+                         : warp_lower_bound(docs, t_first + span * (range + 1) / a.n_ranges);
+    if (doc_hi < doc_lo) doc_hi = doc_lo;
+    const int64_t tok_lo = docs.start(doc_lo), tok_hi = docs.start(doc_hi);
+    int64_t sd[5];
+    sd[0] = doc_lo;
+    sd[4] = doc_hi;
+    for (int q = 1; q < 4; ++q) {
+      int64_t x = warp_lower_bound(docs, tok_lo + (tok_hi - tok_lo) * q / 4);
+      x = x < sd[q - 1] ? sd[q - 1] : x;
+      sd[q] = x > doc_hi ? doc_hi : x;
+    }
+    if (lane == 0) {
+      int64_t tiles = 0;
+      for (int q = 0; q <= 4; ++q) {
+        misc->sub_doc[q] = sd[q];
+        misc->sub_tok[q] = docs.start(sd[q]);
+      }
+      for (int q = 0; q < 4; ++q) {
+        const int64_t t = (misc->sub_tok[q + 1] - misc->sub_tok[q] + 31) / 32;
+        tiles = t > tiles ? t : tiles;
+      }
+      misc->n_tiles = static_cast<int>(tiles);
+    }
+  }
+  // Stage the codebook as fp16 and the query rows as the swizzled B operand (every thread helps).
+  {
+    const int n = a.M * a.K * a.dsub;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float v;
+      if (a.cb_dtype == TMS_F16) v = __half2float(reinterpret_cast<const __half*>(a.codebook)[i]);
+      else if (a.cb_dtype == TMS_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.codebook)[i]);
+      else v = reinterpret_cast<const float*>(a.codebook)[i];
+      cbs[i] = __float2half_rn(v);
+    }
+    const int upr = a.d / 8;  // 16-byte units per query row
+    for (int i = threadIdx.x; i < N * upr; i += blockDim.x) {
+      const int n_row = i / upr, u = i - n_row * upr;
+      const int c = n_row >> 5;
+      const int qi = c / a.nchunk;
+      const int rq = (c - qi * a.nchunk) * 32 + (n_row & 31);
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (rq < a.nq)
+        val = __ldg(reinterpret_cast<const uint4*>(a.Q + (static_cast<int64_t>(qi) * a.nq + rq) * a.d) + u);
+      const uint32_t off = static_cast<uint32_t>((u >> 3) * N * 128 + n_row * 128) +
+                           ((static_cast<uint32_t>(u & 7) ^ static_cast<uint32_t>(n_row & 7)) << 4);
+      *reinterpret_cast<uint4*>(smem + L.b_off + off) = val;
+    }
+    fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&misc->tmem), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = misc->tmem;
+  const uint64_t tmo = a.timeout_ns;
+  const int n_tiles = misc->n_tiles;
+  // slot s: decoded tile at columns [s*acols, (s+1)*acols), accumulator after all the A columns
+  auto a_col = [&](int s) { return static_cast<uint32_t>(s * acols); };
+  auto acc_col = [&](int s) { return static_cast<uint32_t>(S * acols + s * N); };
+
+  if (*abort_flag) {
+    // misaligned shared memory: no role runs (the error word says why)
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(128, N, 0u);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % S;
+        if (!mbar_wait(afull_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 21)) break;
+        tc_fence_after();
+        for (int k = 0; k < a.d / 16; ++k) {
+          const uint64_t bd = sw128_kmajor_desc(b_s + static_cast<uint32_t>((k >> 2) * N * 128 + (k & 3) * 32));
+          mma_f16_ts(tmem_base + acc_col(s), tmem_base + a_col(s) + 8u * k, bd, idesc, k != 0);
+        }
+        mma_commit(accf_bar(s));
+      }
+      // every MMA this thread issued lands before TMEM is released (bounded by time only)
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0, &misc->never, tmo, a.err, 22);
+    }
+  } else if (warp >= kTrDecWarp0 && warp < kTrEpiWarp0) {
+    // ------------------------------------------------------------------ decoders
+    // Warp (q, hp) rebuilds, for every tile, the 64-element column blocks h = hp, hp + 2, ... of
+    // the 32 token rows of lane quarter q (one tcgen05.st of 32 lanes x 32 columns per block).
+    const int q = warp & 3;
+    const int hp = (warp - kTrDecWarp0) >> 2;
+    const int64_t lo = misc->sub_tok[q], hi = misc->sub_tok[q + 1];
+    const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    // d = 128, M = 16, dsub = 8: warp hp needs code bytes [8 hp, 8 hp + 8) of each token
+    const bool fast = (a.M == 16) && (a.dsub == 8) && ((reinterpret_cast<uintptr_t>(a.codes) & 15) == 0);
+    const uint32_t kmax = static_cast<uint32_t>(a.K - 1);
+    auto load_codes = [&](int j) -> uint2 {
+      const int64_t tok = lo + 32LL * j + lane;
+      return (fast && j < n_tiles && tok < hi)
+                 ? __ldg(reinterpret_cast<const uint2*>(a.codes + tok * 16 + 8 * hp))
+                 : make_uint2(0, 0);
+    };
+    // codes of the next two tiles are in flight while this one is decoded
+    uint2 c_n1 = load_codes(0), c_n2 = load_codes(1);
+    bool ok = !(a.debug_flags & 1);
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const uint2 cc = c_n1;
+      c_n1 = c_n2;
+      c_n2 = load_codes(j + 2);
+      const int s = j % S;
+      int w = 0;
+      if (lane == 0) w = mbar_wait(free_bar(s), ((j / S) & 1u) ^ 1u, abort_flag, tmo, a.err, 23);
+      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+      const int64_t tok = lo + 32LL * j + lane;
+      const bool valid = tok < hi;
+      for (int h = hp; h < a.d / 64; h += 2) {
+        uint32_t r[32];
+        if (fast) {  // h == hp: subspaces 8 hp .. 8 hp + 7
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint32_t code = ((i < 4 ? cc.x : cc.y) >> (8 * (i & 3))) & 0xffu;
+            code = min(code, kmax);  // never read past the codebook
+            const uint4 e = *reinterpret_cast<const uint4*>(cbs + ((8 * hp + i) * a.K + code) * 8);
+            r[4 * i] = valid ? e.x : 0u;
+            r[4 * i + 1] = valid ? e.y : 0u;
+            r[4 * i + 2] = valid ? e.z : 0u;
+            r[4 * i + 3] = valid ? e.w : 0u;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int col = 8 * (8 * h + i);  // first element of this 16-byte unit
+            const int m = col / a.dsub, part = col - m * a.dsub;
+            uint4 e = make_uint4(0, 0, 0, 0);
+            if (valid) {
+              const uint32_t code = min(static_cast<uint32_t>(__ldg(a.codes + tok * a.M + m)), kmax);
+              e = *reinterpret_cast<const uint4*>(cbs + (m * a.K + code) * a.dsub + part);
+            }
+            r[4 * i] = e.x;
+            r[4 * i + 1] = e.y;
+            r[4 * i + 2] = e.z;
+            r[4 * i + 3] = e.w;
+          }
+        }
+        tmem_st32(t_quarter + a_col(s) + 32u * h, r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(afull_bar(s));
+    }
+  } else if (warp >= kTrEpiWarp0) {
+    // ------------------------------------------------------------------ epilogue
+    // Lane l keeps, per query row i, the running max acc[c][i] over the tokens of the open
+    // document that sit on lane l (token lo + 32 j + l of every window j). A document's row maxima
+    // need the max across lanes, taken once when the document ends (xpose_max32), not per window.
+    const int q = warp & 3;
+    const int64_t lo = misc->sub_tok[q], hi = misc->sub_tok[q + 1];
+    const int64_t dhi = misc->sub_doc[q + 1];
+    const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    // document ends fetched 32 at a time and handed out with shuffles
+    int64_t e_base = INT64_MIN / 2, ends = 0;
+    auto doc_end = [&](int64_t dd) -> int64_t {
+      if (dd >= dhi) return INT64_MAX;
+      int64_t idx = dd - e_base;
+      if (idx < 0 || idx >= 32) {
+        e_base = dd;
+        const int64_t jj = dd + 1 + lane;
+        ends = (jj <= docs.n_docs) ? docs.start(jj) : INT64_MAX;
+        idx = 0;
+      }
+      return __shfl_sync(0xffffffffu, ends, static_cast<int>(idx));
+    };
+    auto emit = [&](int c, int64_t dd, float x) {
+      const int rq = (c % a.nchunk) * 32 + lane;
+      const float s = warp_sum(rq < a.nq ? x : 0.0f);
+      if (lane == 0) a.out[static_cast<int64_t>(c) * docs.n_docs + dd] = s;
+    };
+    float acc[NCH][32];
+    bool touched[NCH];  // warp-uniform: acc[c] holds tokens of the open document
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      touched[c] = false;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
+    }
+    auto finish = [&](int c, int64_t dd) {
+      const float x = touched[c] ? xpose_max32(acc[c]) : kTrNegInf;
+      emit(c, dd, x);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
+      touched[c] = false;
+    };
+    int64_t doc = misc->sub_doc[q];
+    int64_t dend = doc_end(doc);
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % S;
+      int w = 0;
+      if (lane == 0) w = mbar_wait(accf_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 24);
+      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+      tc_fence_after();
+      const int64_t tb = lo + 32LL * j;
+      const int nv = hi - tb >= 32 ? 32 : (hi > tb ? static_cast<int>(hi - tb) : 0);
+      const int64_t doc0 = doc, dend0 = dend;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t r[32];
+        tmem_ld32_async(t_quarter + acc_col(s) + 32u * c, r);
+        tmem_wait_ld32(r);
+        if (c == NCH - 1) {  // the slot's last read: hand it back before the math
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(free_bar(s));
+        }
+        // the document walk is the same for every chunk: replay it from the window's start
+        doc = doc0;
+        dend = dend0;
+        for (int p = 0; p < nv;) {
+          while (dend <= tb + p) {  // documents that end before this position (empty ones too)
+            finish(c, doc);
+            ++doc;
+            dend = doc_end(doc);
+          }
+          const int64_t e = dend - tb;
+          const int p_hi = e < nv ? static_cast<int>(e) : nv;
+          if (p == 0 && p_hi == 32) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c][i] = fmaxf(acc[c][i], __uint_as_float(r[i]));
+          } else {
+            const bool in = lane >= p && lane < p_hi;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c][i] = in ? fmaxf(acc[c][i], __uint_as_float(r[i])) : acc[c][i];
+          }
+          touched[c] = true;
+          p = p_hi;
+        }
+      }
+    }
+    if (ok) {
+      // the document open at the end of the quarter, then any empty ones after it
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        for (int64_t dd = doc; dd < dhi; ++dd) finish(c, dd);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+__global__ void tr_sum_chunks_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                     int64_t n_queries, int64_t n_docs, int nchunk) {
+  const int64_t total = n_queries * n_docs;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t qq = i / n_docs;
+    const int64_t dd = i - qq * n_docs;
+    float s = 0.0f;
+    for (int p = 0; p < nchunk; ++p) s += partial[(qq * nchunk + p) * n_docs + dd];
+    out[i] = s;
+  }
+}
+
+}  // namespace
+
+size_t pq_tokrows_workspace_size(int64_t n_queries, int64_t nq, int64_t n_docs) {
+  const int64_t nchunk = (nq + 31) / 32;
+  return nchunk > 1 ? align_up(static_cast<size_t>(n_queries * nchunk * n_docs) * 4, 256) : 0;
+}
+
+int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook,
+                      int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
+                      int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
+                      int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
+                      cudaStream_t st) {
+  const int64_t d = M * dsub;
+  const int64_t nchunk = (nq + 31) / 32;
+  const int64_t chunks = n_queries * nchunk;
+  const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2;
+  if (chunks < 1 || chunks > kTrMaxChunks || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
+      K > 256 || cb_bytes > 96 * 1024 || n_tokens <= 0 || (reinterpret_cast<uintptr_t>(Q) & 15))
+    return TMS_ERR_UNSUPPORTED;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  const int N = static_cast<int>(chunks) * 32;
+  const int acols = static_cast<int>(d / 2);
+  // as many slots as TMEM holds: a hand-off through an mbarrier takes ~500 cycles, so several
+  // tiles must be in flight between the decoders, the MMA and the epilogue
+  int nslot = 512 / (acols + N);
+  nslot = static_cast<int>(env_int("TMS_PQ_NSLOT", nslot > 8 ? 8 : nslot));
+  if (nslot < 2 || nslot * (acols + N) > 512) return TMS_ERR_UNSUPPORTED;
+  const size_t need = pq_tokrows_workspace_size(n_queries, nq, n_docs);
+  if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
+  TrArgs a;
+  a.docs.offsets = doc_offsets;
+  a.docs.n_docs = n_docs;
+  a.docs.nd = doc_offsets ? 0 : nd_uniform;
+  a.codes = codes;
+  a.Q = static_cast<const __half*>(Q);
+  a.codebook = codebook;
+  a.out = nchunk > 1 ? static_cast<float*>(workspace) : out;
+  a.err = dev->err_word;
+  a.timeout_ns = wait_timeout_ns();
+  a.cb_dtype = cb_dtype;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.dsub = static_cast<int>(dsub);
+  a.d = static_cast<int>(d);
+  a.nq = static_cast<int>(nq);
+  a.nchunk = static_cast<int>(nchunk);
+  a.n_chunks = static_cast<int>(chunks);
+  a.nslot = nslot;
+  a.debug_flags = debug_flags();
+  // one CTA per SM (a persistent range each), fewer for small corpora
+  int64_t ranges = env_int("TMS_PQ_RANGES", dev->num_sms);
+  const int64_t min_tiles = (n_tokens + 127) / 128;
+  if (ranges > min_tiles) ranges = min_tiles;
+  if (ranges > n_docs) ranges = n_docs;
+  if (ranges < 1) ranges = 1;
+  a.n_ranges = static_cast<int>(ranges);
+  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(cb_bytes), nslot);
+  // at least half the SM's shared memory: one CTA per SM, so the 512-column TMEM allocation
+  // never waits for another CTA
+  size_t smem = L.total;
+  const size_t half = static_cast<size_t>(dev->max_smem_optin) / 2 + 1024;
+  if (smem < half) smem = half;
+  if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
+  auto kern = (chunks == 1) ? pq_tokrows_kernel<1> : pq_tokrows_kernel<2>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return TMS_ERR_CUDA;
+  kern<<<static_cast<unsigned>(ranges), kTrThreads, smem, st>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
+  if (nchunk == 1) return TMS_OK;
+  const int64_t total = n_queries * n_docs;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  tr_sum_chunks_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(workspace), out, n_queries,
+                                               n_docs, static_cast<int>(nchunk));
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace tms

@@ -1,6 +1,8 @@
 """Builds and runs the microbenchmarks in this directory (nvcc, sm_100a; needs a B200).
 
-    python -m tilemaxsim_b200.microbench.run tmem_read
+    python -m tilemaxsim_b200.microbench.run tmem_read    # tcgen05.ld bandwidth per SM
+    python -m tilemaxsim_b200.microbench.run tmem_store   # tcgen05.st bandwidth, alone / beside loads
+    python -m tilemaxsim_b200.microbench.run handoff      # cycles per mbarrier pipeline hand-off
 """
 from __future__ import annotations
 
