@@ -239,6 +239,20 @@ def config_dict(args, cfg) -> dict:
                   else "corpus fits in L2"}
 
 
+def topk_launches(rows: int, n: int, k: int) -> int:
+    """Kernels one tms_topk call launches (csrc/topk.cu: one sort for n <= 16384, else a slice
+    select, plus a merge sort when the row is split into several slices)."""
+    if n <= 16384:
+        return 1
+    c = min(-(-n // 16384), 16384 // k, 1 if rows >= 296 else 296 // rows)
+    return 2 if c >= 2 else 1
+
+
+def search_launches(rows: int, n: int, k: int, world: int, score_launches: int) -> int:
+    """Our kernels per search step: scoring, local top-k, and (N > 1) the merge top-k."""
+    return score_launches + topk_launches(rows, n, k) + (topk_launches(rows, world * k, k) if world > 1 else 0)
+
+
 PQ_CONFIGS = {
     # name: (n_queries, nq, M, K, dsub, n_docs per GPU, nd, k) -- BASELINE config 4
     "c4": (16, 32, 16, 256, 8, 1_000_000, 128, 100),
@@ -246,6 +260,16 @@ PQ_CONFIGS = {
     # single-query PQ over the same corpus (the north star's single-query PQ path)
     "q1_pq": (1, 32, 16, 256, 8, 1_000_000, 128, 100),
 }
+
+
+def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int) -> int:
+    """Kernels one default-mode PQ scoring call launches (csrc/pq_adc.cu routing): the token-rows
+    kernel for 1-2 query chunks, else query packing + the decoder-warp dense kernel; plus the chunk
+    sum when Nq > 32."""
+    chunks = nqry * -(-nq // 32)
+    d = M * dsub
+    tokrows = chunks <= 2 and d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256
+    return (1 if tokrows else 2) + (1 if nq > 32 else 0)
 
 
 def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
@@ -312,6 +336,9 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
     clocks = clk.summary()
     tmem_peak = 56.0 * torch.cuda.get_device_properties(device).multi_processor_count * \
         (ClockSampler.last_sm_mhz or 1965.0) * 1e6 / 1e9
+    gather_bytes = float(T) * M * dsub * 2
+    smem_peak = 128.0 * torch.cuda.get_device_properties(device).multi_processor_count * \
+        (ClockSampler.last_sm_mhz or 1965.0) * 1e6 / 1e9
     print(json.dumps({
         "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -329,10 +356,15 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
                      "hbm": {"achieved_gbs": code_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": pk["hbm_gbs"]},
                      "tmem_read": {"achieved_gbs": tmem_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
                                    "frac": tmem_bytes / (kern_ms * 1e-3) / 1e9 / tmem_peak},
+                     # decoding reads one codebook row (dsub fp16) per code from shared memory:
+                     # T*M*dsub*2 bytes per launch at least, against 128 B/clk per SM
+                     "smem_gather": {"achieved_gbs": gather_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": smem_peak,
+                                     "frac": gather_bytes / (kern_ms * 1e-3) / 1e9 / smem_peak},
                      "note": "LUT lookups/s counts the table-lookup equivalent (B_q*Nq*T*M) of the work"},
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s", "h2d_bytes_per_step": Qh.numel() * 2,
                 "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
-        "gpu_launches": 3 * args.steps, "clocks": clocks}), flush=True)
+        "gpu_launches": search_launches(nqry, n_docs, k, world, pq_score_launches(nqry, nq, M, K, dsub)) * args.steps,
+        "clocks": clocks}), flush=True)
 
 
 def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
@@ -427,7 +459,8 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     tf = ROOT / "profiles" / f"dense_maxsim_{args.config}_traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
-    launches_per_step = 3 + (1 if world > 1 else 0) + (1 if nq > 32 else 0)
+    # query packing + the dense kernel (+ the chunk sum for Nq > 32), then the top-k kernels
+    launches_per_step = search_launches(nqry, n_docs, k, world, 2 + (1 if nq > 32 else 0))
     out = {
         "metric": "doc-tokens scored/s", "value": value, "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
