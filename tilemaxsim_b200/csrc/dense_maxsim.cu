@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc(128, TN, a.ab_format);
+      const bool skip_mma = (a.debug_flags & 8) != 0;
       bool ok = true;
       if (QRES && tok_hi > tok_lo) ok = mbar_wait(qfull_bar, 0, abort_flag, tmo, a.err, 3);
       int s = 0;
@@ -397,15 +398,18 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
               a_base = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
               b_base = a_base + kQChunkBytes;
             }
+            // descriptors of the 4 K slices of this chunk: the start address field counts
+            // 16-byte units, so each 32-byte K step adds 2
+            const uint64_t ad0 = sw128_kmajor_desc(a_base);
+            const uint64_t bd0 = sw128_kmajor_desc(b_base);
+            if (!skip_mma) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if (a.debug_flags & 8) break;
-              const uint64_t ad = sw128_kmajor_desc(a_base + 32u * k);
-              const uint64_t bd = sw128_kmajor_desc(b_base + 32u * k);
-              if (TF32)
-                mma_tf32(d_tmem, ad, bd, idesc, (c | k) != 0);
-              else
-                mma_f16(d_tmem, ad, bd, idesc, (c | k) != 0);
+              for (int k = 0; k < 4; ++k) {
+                if (TF32)
+                  mma_tf32(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
+                else
+                  mma_f16(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
+              }
             }
             if (!QRES) {
               mma_commit(empty_bar(s));
