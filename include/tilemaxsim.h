@@ -115,8 +115,10 @@ TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, i
 /* codes: (n_tokens, M) uint8, doc layout as in tms_dense_maxsim (offsets or nd_uniform).
  * out[q * n_docs + doc] = sum_i max_j sum_m table[q,i,m,codes[j,m]] (K <= 256).
  * mode TMS_PQ_FAST: fp16 queries with dsub % 8 == 0, M*dsub % 64 == 0 and a codebook of <= 96 KB
- * in fp16 run on the tensor cores (codes decoded in shared memory through the codebook rounded to
- * fp16, never written to HBM; |error| <= 1e-3*|score| + 5e-3); other shapes fall back to:
+ * in fp16 run on the tensor cores (codes decoded on chip through the codebook rounded to fp16,
+ * never written to HBM; |error| <= 1e-3*|score| + 5e-3): up to two 32-row query chunks
+ * (n_queries * ceil(nq / 32) <= 2, d <= 256) with the decoded tokens written to tensor memory,
+ * larger batches with the tokens decoded into shared memory; other shapes fall back to:
  * mode TMS_PQ_EXACT: the fp32 distance table is built in shared memory and table entries are
  * summed in m order (the reference's arithmetic). The workspace must be 1024-byte aligned. */
 TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
