@@ -451,7 +451,7 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
         ach = bytes_launch / (dense_ms * 1e-3) / 1e9
         peak, unit = pk["hbm_gbs"], "GB/s"
     # The epilogue reads every fp32 similarity once from TMEM: B_q*Nq*T values per launch. TMEM ->
-    # register bandwidth measured at ~56 B/clk per SM (profiles/tmem_read_bandwidth.md).
+    # register bandwidth measured at ~56 B/clk per SM (tilemaxsim_b200/microbench/tmem_read.cu).
     tmem_bytes = 4.0 * nqry * nq * (T_total / world)
     clk = ClockSampler.last_sm_mhz or 1965.0
     tmem_peak = 56.0 * torch.cuda.get_device_properties(device).multi_processor_count * clk * 1e6 / 1e9
@@ -477,8 +477,8 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
                      "algorithmic": {"flops_per_launch": flops_launch, "bytes_per_launch": bytes_launch},
                      "tmem_read": {"achieved_gbs": tmem_bytes / (dense_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
                                    "frac": tmem_bytes / (dense_ms * 1e-3) / 1e9 / tmem_peak,
-                                   "note": "epilogue reads B_q*Nq*T fp32 values from TMEM; peak = 56 B/clk/SM "
-                                           "measured (profiles/tmem_read_bandwidth.md) x SMs x median SM clock"}},
+                                   "note": "epilogue reads B_q*Nq*T fp32 values from TMEM; peak = 56 B/clk/SM ("
+                                           "measured by tilemaxsim_b200/microbench/tmem_read.cu) x SMs x median SM clock"}},
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s",
                 "h2d_bytes_per_step": Qh.numel() * Qh.element_size(),
                 "d2h_bytes_per_step": nqry * k * (4 + 8), "ms_per_step": e2e_ms},
