@@ -129,6 +129,28 @@ def test_pq_small_batch_token_rows(nqry, M, K, dsub, nq, lengths, cuda_device):
     np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=5e-3)
 
 
+@pytest.mark.parametrize("nqry", [1, 2, 5])
+def test_pq_offsets_not_starting_at_zero_and_empty_corpus(nqry, cuda_device):
+    """A corpus given as a window of a larger code array (offsets start past 0), and a corpus of
+    empty documents only (every score -inf), on every PQ kernel the query count selects."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    cb = R.randn((16, 256, 8), 3, torch.float32)
+    Qb = R.normalized((nqry, 32, 128), 4)
+    lens = R.ragged_lengths(300, 0, 150, seed=11)
+    off = R.offsets_from_lengths(lens) + 777
+    codes = torch.randint(0, 256, (int(off[-1]) + 50, 16), generator=R.gen(5), dtype=torch.uint8)
+    pq = TileMaxSimPQ(cb.to(cuda_device))
+    got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device),
+                           torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=5e-3)
+    empty = torch.full((41,), 5, dtype=torch.int64)
+    s = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device), empty.to(cuda_device)).cpu()
+    assert s.shape == (nqry, 40) and torch.all(torch.isneginf(s))
+
+
 def test_pq_single_query_full_size_property(cuda_device):
     """Single query over a 400k-document slice of BASELINE config 4 (51.2M code rows) on the
     token-rows kernel agrees with the exact table-lookup path on every score."""
