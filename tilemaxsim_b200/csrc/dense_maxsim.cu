@@ -749,6 +749,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
           if (!(ok = wait_full(slot, u))) break;
           tc_fence_after();
           const int chunk = (m_first + m) * 4 + lg;
+          bool released = false;
           if (chunk < a.n_chunks_total && !skip_math) {
             float rm = carry[m * kQTileRows + row];
             int64_t dd = doc, de = dend;
@@ -783,6 +784,14 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
             };
             // TMEM loads double-buffered (block b+1 in flight while b is reduced): 64 columns
             // per load, 32 in the PQ variant (448 threads leave it fewer registers)
+            // The slot goes back to the MMA as soon as its last block is in registers, before
+            // that block is reduced: the reduction then overlaps the slot's refill.
+            auto release_slot = [&]() {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(acce_bar(slot));
+              released = true;
+            };
             if constexpr (!PQ) {
               uint32_t ra[64], rb[64];
               tmem_ld64_async(tbase, ra);
@@ -794,6 +803,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
                 if (cb < ncol) {
                   tmem_wait_ld(cur);
                   if (b + 1 < TN / 64 && cb + 64 < ncol) tmem_ld64_async(tbase + cb + 64, nxt);
+                  else release_slot();
                   reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[0]), cb);
                   if (cb + 32 < ncol) reduce32(*reinterpret_cast<const uint32_t(*)[32]>(&cur[32]), cb + 32);
                 }
@@ -809,6 +819,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
                 if (cb < ncol) {
                   tmem_wait_ld32(cur);
                   if (b + 1 < TN / 32 && cb + 32 < ncol) tmem_ld32_async(tbase + cb + 32, nxt);
+                  else release_slot();
                   reduce32(cur, cb);
                 }
               }
@@ -817,9 +828,11 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
             next_doc = dd;
             next_dend = de;
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acce_bar(slot));
+          if (!released) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce_bar(slot));
+          }
         }
         doc = next_doc;
         dend = next_dend;
