@@ -67,3 +67,17 @@ def test_topk_ties():
     np.testing.assert_array_equal(ids, g["order"])
     np.testing.assert_array_equal(vals[:, :100][~np.isnan(vals[:, :100])],
                                   g["torch_topk_values"][~np.isnan(vals[:, :100])])
+
+
+def test_segment_max_ignores_rows_past_the_last_document():
+    """Rows after the last offset (a corpus window inside a larger token array) belong to no
+    document; empty documents score -inf."""
+    S = np.arange(10, dtype=np.float32).reshape(10, 1)
+    got = O._segment_max(S, np.array([2, 4, 4, 6]), 0).ravel()
+    np.testing.assert_array_equal(got, np.array([3, -np.inf, 5], np.float32))
+    codes = np.zeros((12, 2), np.uint8)
+    codes[10:] = 1  # trailing rows with a larger table entry must not reach the last document
+    table = np.zeros((1, 2, 2), np.float32)
+    table[:, :, 1] = 100.0
+    tok = O.pq_token_scores(table, codes)
+    np.testing.assert_array_equal(O._segment_max(tok, np.array([0, 5, 10]), 0).ravel(), [0, 0])
