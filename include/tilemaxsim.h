@@ -127,6 +127,25 @@ TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t
                           int64_t n_docs, int64_t nd_uniform, float* out, int mode,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- scoring + top-k, bounded memory */
+
+/* Workspace for tms_dense_maxsim_topk with the same arguments (0 = unsupported shape). */
+TMS_API size_t tms_dense_topk_workspace_size(int dtype, int64_t n_queries, int64_t nq, int64_t d,
+                                             int64_t n_docs, int64_t k, int64_t chunk_docs);
+
+/* Scores the corpus as tms_dense_maxsim does and writes each query's k best documents
+ * (score descending, id ascending, NaN last; ids = document index + id_base) to out_vals
+ * (n_queries, k) fp32 and out_ids (n_queries, k) int64, never holding more than chunk_docs
+ * documents' scores (chunk_docs <= 0: a 1 GiB score buffer). The result equals tms_topk over the
+ * full score matrix. k <= 2048 and k <= n_docs. The workspace must be 1024-byte aligned.
+ * Replaces torch.topk over the full score matrix (reference src/cycle3_experiments.py:215). */
+TMS_API int tms_dense_maxsim_topk(const void* Q, int dtype, int64_t n_queries, int64_t nq,
+                                  int64_t d, const void* D, int64_t n_tokens,
+                                  const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                                  int64_t k, int64_t chunk_docs, int64_t id_base, float* out_vals,
+                                  int64_t* out_ids, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
 /* ---------------------------------------------------------------- top-k */
 
 TMS_API size_t tms_topk_workspace_size(int64_t rows, int64_t n, int64_t k);

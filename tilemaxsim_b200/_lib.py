@@ -46,6 +46,9 @@ SIGNATURES = {
     "tms_pq_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "tms_pq_maxsim": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64,
                              _i64, _vp, _i32, _vp, _sz, _vp]),
+    "tms_dense_topk_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "tms_dense_maxsim_topk": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
+                                     _i64, _vp, _vp, _vp, _sz, _vp]),
     "tms_topk_workspace_size": (_sz, [_i64, _i64, _i64]),
     "tms_topk": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _sz, _vp]),
 }

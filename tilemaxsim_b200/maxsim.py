@@ -129,8 +129,48 @@ def topk(scores: torch.Tensor, k: int, ids: torch.Tensor | None = None, id_base:
 
 
 def maxsim_topk(Qb: torch.Tensor, D_tokens: torch.Tensor, doc_offsets: torch.Tensor, k: int,
-                id_base: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+                id_base: int = 0, chunk_docs: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Scores B_q queries against a ragged corpus and returns each query's k best documents:
-    (scores (B_q, k) fp32, doc ids (B_q, k) int64), ties broken by the smaller doc id."""
-    scores = maxsim_batched(Qb, D_tokens, doc_offsets)
-    return topk(scores, k, id_base=id_base)
+    (scores (B_q, k) fp32, doc ids (B_q, k) int64), ties broken by the smaller doc id.
+
+    The full (B_q, n) score matrix is never held: documents are scored `chunk_docs` at a time
+    (default: a 1 GiB score buffer) and each chunk's top-k is merged into a running list, which
+    gives exactly the top-k of the full matrix (tms_dense_maxsim_topk)."""
+    lib = _lib.load()
+    single = Qb.dim() == 2
+    if single:
+        Qb = Qb.unsqueeze(0)
+    dev = _lib.require_cuda(Qb, D_tokens, doc_offsets)
+    if Qb.dim() != 3 or D_tokens.dim() != 2 or doc_offsets.dim() != 1 or doc_offsets.numel() < 1:
+        raise ValueError("expected Q (B_q, Nq, d), D (T, d) and 1-D offsets (n_docs + 1,)")
+    Bq, Nq, d = Qb.shape
+    if D_tokens.shape[1] != d:
+        raise ValueError(f"embedding dims differ: Q has d={d}, D has d={D_tokens.shape[1]}")
+    if D_tokens.dtype not in _lib.DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {D_tokens.dtype}; use float16, bfloat16 or float32")
+    n_docs = doc_offsets.numel() - 1
+    if not (0 < k <= n_docs):
+        raise ValueError(f"k={k} must be in [1, n_docs={n_docs}]")
+    Qb = _as_contig(Qb.to(D_tokens.dtype))
+    D_tokens = _as_contig(D_tokens)
+    doc_offsets = _as_contig(doc_offsets.to(torch.int64))
+    dt = _lib.DTYPE_CODE[D_tokens.dtype]
+    chunk = 0 if chunk_docs is None else int(chunk_docs)
+    with torch.cuda.device(dev):
+        vals = torch.empty((Bq, k), dtype=torch.float32, device=dev)
+        ids = torch.empty((Bq, k), dtype=torch.int64, device=dev)
+        if Bq > 0:
+            ws_bytes = lib.tms_dense_topk_workspace_size(dt, Bq, Nq, d, n_docs, k, chunk)
+            if ws_bytes == 0:
+                raise _lib.TileMaxSimError(_lib.TMS_ERR_UNSUPPORTED, f"dense MaxSim top-k with d={d}")
+            ws, ws_ptr = _lib.workspace(ws_bytes, dev)
+            rc = lib.tms_dense_maxsim_topk(
+                ctypes.c_void_p(Qb.data_ptr()), dt, Bq, Nq, d, ctypes.c_void_p(D_tokens.data_ptr()),
+                D_tokens.shape[0], ctypes.c_void_p(doc_offsets.data_ptr()), n_docs, 0, k, chunk, id_base,
+                ctypes.c_void_p(vals.data_ptr()), ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(ws_ptr),
+                ws_bytes, ctypes.c_void_p(_lib.stream_handle(dev)))
+            _lib.check(rc, "tms_dense_maxsim_topk")
+            del ws
+    if single:
+        return vals[0], ids[0]
+    return vals, ids

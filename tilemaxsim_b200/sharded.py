@@ -23,11 +23,12 @@ PAD_ID = torch.iinfo(torch.int64).max
 
 
 def _pad_to_k(vals: torch.Tensor, ids: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Pads (rows, kk) lists to k columns with (-inf, PAD_ID), which rank after every real entry."""
+    """Pads (rows, kk) lists to k columns with (NaN, PAD_ID), which rank after every real entry
+    (NaN ranks last, and among NaN the padding's id is the largest)."""
     rows, kk = vals.shape
     if kk == k:
         return vals.contiguous(), ids.contiguous()
-    pv = torch.full((rows, k), float("-inf"), dtype=vals.dtype, device=vals.device)
+    pv = torch.full((rows, k), float("nan"), dtype=vals.dtype, device=vals.device)
     pi = torch.full((rows, k), PAD_ID, dtype=ids.dtype, device=ids.device)
     pv[:, :kk] = vals
     pi[:, :kk] = ids
