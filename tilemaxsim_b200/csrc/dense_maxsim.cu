@@ -73,6 +73,7 @@ struct DenseArgs {
   uint32_t ab_format;  // MMA operand format: 0 = f16, 1 = bf16, 2 = tf32
   // PQ variant: D rows are decoded from codes (n_tokens, M) through codebook (M, K, dsub)
   const uint8_t* codes;
+  int64_t n_code_rows;  // PQ variant: rows of codes; its token range is clamped to them
   const void* codebook;
   int cb_dtype, pq_M, pq_K, pq_dsub;
   uint32_t cb_bytes;   // fp16 codebook bytes staged in shared memory (0 for the dense kernel)
@@ -222,6 +223,10 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
       rinfo->doc_hi = doc_hi;
       rinfo->tok_lo = a.docs.start(doc_lo);
       rinfo->tok_hi = (doc_hi > doc_lo) ? a.docs.start(doc_hi) : a.docs.start(doc_lo);
+      if (PQ) {  // decoders read codes rows [tok_lo, tok_hi): keep them inside the array
+        rinfo->tok_lo = max(min(rinfo->tok_lo, a.n_code_rows), int64_t(0));
+        rinfo->tok_hi = max(min(rinfo->tok_hi, a.n_code_rows), rinfo->tok_lo);
+      }
       prefetch_tmap(&dmap);
       prefetch_tmap(&qmap);
     }
@@ -1130,6 +1135,7 @@ extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int
   args.out_mode = out_mode;
   args.ab_format = (dtype == TMS_F16) ? 0u : (dtype == TMS_BF16) ? 1u : 2u;
   args.codes = nullptr;
+  args.n_code_rows = 0;
   args.codebook = nullptr;
   args.cb_dtype = args.pq_M = args.pq_K = args.pq_dsub = 0;
   args.cb_bytes = 0;
@@ -1237,6 +1243,7 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
   args.out_mode = TMS_OUT_SCORE;
   args.ab_format = 0u;
   args.codes = codes;
+  args.n_code_rows = n_tokens;
   args.codebook = codebook;
   args.cb_dtype = cb_dtype;
   args.pq_M = static_cast<int>(M);

@@ -56,6 +56,7 @@ struct PqArgs {
   const void* Q;
   const void* cb;
   const uint8_t* codes;
+  int64_t n_tokens;  // rows of codes: token ranges are clamped to [0, n_tokens)
   DocLayout docs;
   float* out;  // (n_queries * nslice, n_docs): slice partial scores (final scores if nslice == 1)
   int q_dtype, cb_dtype;
@@ -100,7 +101,9 @@ __global__ void __launch_bounds__(kPqThreads)
   const int ns = min(QS, a.nq - i0);
   const uint32_t kmax = static_cast<uint32_t>(a.K - 1);
   for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
-    const int64_t t_lo = a.docs.start(doc), t_hi = a.docs.start(doc + 1);
+    // clamped to the code rows that exist, so malformed offsets never read outside `codes`
+    const int64_t t_lo = max(min(a.docs.start(doc), a.n_tokens), int64_t(0));
+    const int64_t t_hi = max(min(a.docs.start(doc + 1), a.n_tokens), t_lo);
     float run[QS];
 #pragma unroll
     for (int s = 0; s < QS; ++s) run[s] = kNegInfPq;
@@ -277,6 +280,7 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   a.Q = Q;
   a.cb = codebook;
   a.codes = codes;
+  a.n_tokens = n_tokens;
   a.docs.offsets = doc_offsets;
   a.docs.n_docs = n_docs;
   a.docs.nd = doc_offsets ? 0 : nd_uniform;

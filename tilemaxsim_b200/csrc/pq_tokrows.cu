@@ -49,6 +49,7 @@ constexpr float kTrNegInf = -__builtin_huge_valf();
 struct TrArgs {
   DocLayout docs;
   const uint8_t* codes;
+  int64_t n_tokens;  // rows of codes: the quarters' token ranges are clamped to [0, n_tokens)
   const __half* Q;  // (n_queries, nq, d) fp16
   const void* codebook;
   float* out;  // (n_chunks, n_docs): final scores when nchunk == 1, else per-chunk partials
@@ -154,9 +155,14 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     }
     if (lane == 0) {
       int64_t tiles = 0;
+      int64_t prev = 0;
       for (int q = 0; q <= 4; ++q) {
         misc->sub_doc[q] = sd[q];
-        misc->sub_tok[q] = docs.start(sd[q]);
+        // clamped (and kept non-decreasing) so malformed offsets never read outside `codes`
+        int64_t t = docs.start(sd[q]);
+        t = t < prev ? prev : (t > a.n_tokens ? a.n_tokens : t);
+        misc->sub_tok[q] = t;
+        prev = t;
       }
       for (int q = 0; q < 4; ++q) {
         const int64_t t = (misc->sub_tok[q + 1] - misc->sub_tok[q] + 31) / 32;
@@ -445,6 +451,7 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   a.docs.n_docs = n_docs;
   a.docs.nd = doc_offsets ? 0 : nd_uniform;
   a.codes = codes;
+  a.n_tokens = n_tokens;
   a.Q = static_cast<const __half*>(Q);
   a.codebook = codebook;
   a.out = nchunk > 1 ? static_cast<float*>(workspace) : out;
