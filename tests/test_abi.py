@@ -72,3 +72,21 @@ def test_dense_plans():
     assert nm == 16 and qres == 1 and g * ng >= nm and ctas % 148 == 0 and smem <= 232448
     assert lib.tms_dense_plan_info(0, 16, 32, 768, 50_000, 12_800_000, 0, 148, info) == 0
     assert info[1] == 0 and info[8] <= 232448
+
+
+def test_dense_topk_workspace_is_bounded_by_the_chunk():
+    """tms_dense_topk_workspace_size: the score buffer scales with chunk_docs, not with the corpus;
+    0 for arguments no call could take (host-side sizing, no GPU needed)."""
+    from tilemaxsim_b200 import _lib
+    lib = _lib.load()
+    f = lib.tms_dense_topk_workspace_size
+    small = f(_lib.TMS_F16, 64, 32, 128, 10_000_000, 100, 5000)
+    big = f(_lib.TMS_F16, 64, 32, 128, 10_000_000, 100, 50_000)
+    assert 0 < small < big
+    assert big - small >= 64 * 45_000 * 4  # the (B_q, chunk) fp32 score buffer grows with the chunk
+    assert small < 64 * 5000 * 4 + (8 << 20)  # scores + query tiles + candidate lists, no corpus term
+    default = f(_lib.TMS_F16, 256, 32, 128, 10_000_000, 100, 0)
+    assert (1 << 30) <= default < (1 << 30) + (16 << 20)  # the 1 GiB default score buffer
+    assert f(_lib.TMS_F16, 64, 32, 128, 0, 100, 0) == 0
+    assert f(_lib.TMS_F16, 64, 32, 128, 1000, 0, 0) == 0
+    assert f(_lib.TMS_F16, 0, 32, 128, 1000, 10, 0) == 0
