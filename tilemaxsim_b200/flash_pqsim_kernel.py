@@ -2,12 +2,14 @@
 
 ``TileMaxSimPQ(codebook)`` keeps the reference's attributes (``codebook, M, K, dsub, d``) and
 methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_pqsim_kernel.py:
-176-280). Scoring runs in the sm_100a ADC kernel (C ABI ``tms_pq_maxsim``): each CTA builds its
-query slice's distance table in shared memory and scores straight from the uint8 codes, so neither
-the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote both).
-``score_queries`` is the additive multi-query, ragged-corpus entry point. By default fp16 queries
-run on the tensor cores: codes are decoded through a shared-memory fp16 codebook straight into the
-MMA operand tiles of the dense kernel (``exact=True`` keeps the table-lookup arithmetic).
+176-280). Scoring goes through the C ABI ``tms_pq_maxsim`` and reads the uint8 codes directly:
+neither the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote
+both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default fp16
+queries run on the tensor cores, each token rebuilt on chip from an fp16 copy of the codebook: for
+one or two 32-row query chunks the rebuilt tokens go to tensor memory as the MMA's A operand
+(token-rows kernel), for larger batches into the dense kernel's shared-memory operand tiles.
+``exact=True`` (and any shape the tensor path does not take) uses the table-lookup kernel: each
+CTA builds its query slice's fp32 distance table in shared memory, the reference's arithmetic.
 ``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
 """
 from __future__ import annotations
@@ -32,9 +34,10 @@ class TileMaxSimPQ:
         """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256.
 
         exact=False (default): fp16 queries of a supported shape are scored on the tensor cores,
-        codes decoded in shared memory through the codebook rounded to fp16
-        (|error| <= 1e-3*|score| + 5e-3). exact=True: fp32 table lookups, the reference's
-        arithmetic (also used automatically for shapes the tensor path does not take)."""
+        codes decoded on chip through the codebook rounded to fp16 (|error| <= 1e-3*|score| +
+        5e-3); fp32 / bf16 queries take the exact path. exact=True: fp32 table lookups, the
+        reference's arithmetic (also used automatically for shapes the tensor path does not
+        take)."""
         self.exact = bool(exact)
         self.codebook = codebook.contiguous()
         self.M, self.K, self.dsub = codebook.shape
