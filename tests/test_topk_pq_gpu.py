@@ -151,6 +151,25 @@ def test_pq_offsets_not_starting_at_zero_and_empty_corpus(nqry, cuda_device):
     assert s.shape == (nqry, 40) and torch.all(torch.isneginf(s))
 
 
+@pytest.mark.parametrize("qdtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("nqry", [1, 5])
+def test_pq_fast_mode_rounds_wider_queries_to_fp16(qdtype, nqry, cuda_device):
+    """Fast mode takes fp32 / bf16 queries on the tensor-core path (rounded to fp16) and stays
+    within the fast-mode tolerance of the fp32 table-lookup oracle."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    lens = R.ragged_lengths(300, 0, 150, seed=21)
+    off = R.offsets_from_lengths(lens)
+    cb = R.randn((16, 256, 8), 3, torch.float32)
+    Qb = R.normalized((nqry, 32, 128), 4).float().to(qdtype)
+    codes = torch.randint(0, 256, (int(off[-1]), 16), generator=R.gen(5), dtype=torch.uint8)
+    got = TileMaxSimPQ(cb.to(cuda_device)).score_queries(
+        Qb.to(cuda_device), codes.to(cuda_device), torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.pq_maxsim_adc_ragged(Qb.float(), cb, codes, off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=5e-3)
+
+
 def test_pq_single_query_full_size_property(cuda_device):
     """Single query over a 400k-document slice of BASELINE config 4 (51.2M code rows) on the
     token-rows kernel agrees with the exact table-lookup path on every score."""

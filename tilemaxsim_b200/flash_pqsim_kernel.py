@@ -4,10 +4,11 @@
 methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_pqsim_kernel.py:
 176-280). Scoring goes through the C ABI ``tms_pq_maxsim`` and reads the uint8 codes directly:
 neither the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote
-both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default fp16
-queries run on the tensor cores, each token rebuilt on chip from an fp16 copy of the codebook: for
-one or two 32-row query chunks the rebuilt tokens go to tensor memory as the MMA's A operand
-(token-rows kernel), for larger batches into the dense kernel's shared-memory operand tiles.
+both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default the
+queries run on the tensor cores in fp16 (fp32 / bf16 ones are rounded to fp16), each token rebuilt
+on chip from an fp16 copy of the codebook: for one or two 32-row query chunks the rebuilt tokens go
+to tensor memory as the MMA's A operand (token-rows kernel), for larger batches into the dense
+kernel's shared-memory operand tiles.
 ``exact=True`` (and any shape the tensor path does not take) uses the table-lookup kernel: each
 CTA builds its query slice's fp32 distance table in shared memory, the reference's arithmetic.
 ``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
@@ -33,17 +34,23 @@ class TileMaxSimPQ:
     def __init__(self, codebook: torch.Tensor, exact: bool = False):
         """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256.
 
-        exact=False (default): fp16 queries of a supported shape are scored on the tensor cores,
-        codes decoded on chip through the codebook rounded to fp16 (|error| <= 1e-3*|score| +
-        5e-3); fp32 / bf16 queries take the exact path. exact=True: fp32 table lookups, the
-        reference's arithmetic (also used automatically for shapes the tensor path does not
-        take)."""
+        exact=False (default): queries of a supported shape are scored on the tensor cores in
+        fp16 (fp32 / bf16 queries are rounded to fp16), codes decoded on chip through the
+        codebook rounded to fp16 (|error| <= 1e-3*|score| + 5e-3). exact=True: fp32 table
+        lookups, the reference's arithmetic (also used automatically for shapes the tensor path
+        does not take)."""
         self.exact = bool(exact)
         self.codebook = codebook.contiguous()
         self.M, self.K, self.dsub = codebook.shape
         self.d = self.M * self.dsub
         if self.codebook.dtype not in _lib.DTYPE_CODE:
             raise TypeError(f"codebook dtype {codebook.dtype} not supported")
+
+    def _tensor_shape(self) -> bool:
+        """The tensor-core path's shape rule (csrc: pq_mma_codebook_bytes): dsub % 8 == 0,
+        d % 64 == 0, d <= 512, K <= 256 and an fp16 codebook of at most 96 KB."""
+        return (self.dsub % 8 == 0 and self.d % 64 == 0 and self.d <= 512 and self.K <= 256
+                and self.M * self.K * self.dsub * 2 <= 96 * 1024)
 
     def _q(self, Q: torch.Tensor) -> torch.Tensor:
         if Q.dtype not in _lib.DTYPE_CODE:
@@ -78,6 +85,8 @@ class TileMaxSimPQ:
         if codes_tokens.shape[-1] != self.M:
             raise ValueError(f"codes have {codes_tokens.shape[-1]} sub-quantizers, codebook has {self.M}")
         Qb = self._q(Qb)
+        if not self.exact and Qb.dtype != torch.float16 and self._tensor_shape():
+            Qb = Qb.half()  # the tensor-core path multiplies fp16 queries (fast-mode tolerance)
         codes_tokens = _codes_u8(codes_tokens)
         with torch.cuda.device(dev):
             out = torch.empty(Bq, n_docs, dtype=torch.float32, device=dev)
