@@ -39,7 +39,8 @@ class GraphedStep:
             cur.wait_stream(side)
             torch.cuda.synchronize(dev)
             self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph):
+            # thread-local capture: CUDA calls other threads make meanwhile are not restricted
+            with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
                 out = fn(*self.inputs)
         self.single = isinstance(out, torch.Tensor)
         self.outputs = [out] if self.single else list(out)
