@@ -43,6 +43,8 @@ extern "C" {
 #define TMS_ERR_TIMEOUT 4     /* a bounded device-side wait gave up (reported by tms_last_device_error) */
 #define TMS_ERR_WORKSPACE 5   /* workspace smaller than the *_workspace_size query */
 #define TMS_ERR_TOO_LARGE 6   /* problem needs more scratch than tms_dense_maxsim_noalloc holds */
+#define TMS_ERR_BAD_OFFSETS 7 /* document offsets negative, decreasing or past n_tokens
+                                 (found by tms_validate_offsets, reported by tms_last_device_error) */
 
 /* element types */
 #define TMS_F16 0
@@ -60,9 +62,19 @@ extern "C" {
 TMS_API const char* tms_strerror(int code);
 TMS_API const char* tms_version(void);
 
-/* Reads and clears the device-side error word (set by bounded waits that timed out). Synchronises
- * `stream`. Returns TMS_OK or TMS_ERR_TIMEOUT; *detail (may be NULL) receives the raw word. */
+/* Reads and clears the device-side error word (bit 31: a bounded wait timed out, low bits = the
+ * wait's site; bit 30: tms_validate_offsets found a bad entry, low bits = its index). Synchronises
+ * `stream`. Returns TMS_OK, TMS_ERR_TIMEOUT or TMS_ERR_BAD_OFFSETS; *detail (may be NULL)
+ * receives the raw word. */
 TMS_API int tms_last_device_error(void* stream, uint32_t* detail);
+
+/* Checks a document offsets array on the device, asynchronously on `stream`: every entry of
+ * offsets[0..n_docs] must be >= 0 and <= n_tokens and the array non-decreasing. A violation sets
+ * the device error word (read it with tms_last_device_error). The scoring calls do not run this
+ * check themselves (it would cost a host synchronisation per call); whatever the offsets, they
+ * never read outside D or the codes array. */
+TMS_API int tms_validate_offsets(const int64_t* doc_offsets, int64_t n_docs, int64_t n_tokens,
+                                 void* stream);
 
 /* ---------------------------------------------------------------- dense MaxSim (tcgen05 + TMA) */
 

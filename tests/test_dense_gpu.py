@@ -202,3 +202,23 @@ def test_bounded_wait_reports_timeout(case, cuda_device):
     # the context still works and the error word was cleared
     close(run(), want, *tol)
     assert _lib.last_device_error(cuda_device)[0] == _lib.TMS_OK
+
+
+def test_validate_offsets(cuda_device, monkeypatch):
+    """tms_validate_offsets flags negative, decreasing and out-of-range offsets through the device
+    error word (then cleared); TMS_CHECK_OFFSETS=1 runs it before ragged scoring, so malformed
+    offsets raise on the host before any scoring kernel is launched."""
+    from tilemaxsim_b200 import _lib, maxsim_batched, validate_offsets
+    t = lambda x: torch.tensor(x, dtype=torch.int64, device=cuda_device)  # noqa: E731
+    validate_offsets(t([0, 3, 3, 10]), 10)
+    validate_offsets(t([4, 4]), 10)
+    for bad, idx in (([0, 5, 3, 10], 2), ([0, 3, 12], 2), ([-1, 3], 0)):
+        with pytest.raises(ValueError, match=rf"doc_offsets\[{idx}\]"):
+            validate_offsets(t(bad), 10)
+        assert _lib.last_device_error(cuda_device)[0] == _lib.TMS_OK  # read and cleared
+    Q = R.normalized((2, 32, 128), 5).to(cuda_device)
+    D = R.normalized((10, 128), 6).to(cuda_device)
+    monkeypatch.setenv("TMS_CHECK_OFFSETS", "1")
+    with pytest.raises(ValueError):
+        maxsim_batched(Q, D, t([0, 5, 3, 10]))
+    assert maxsim_batched(Q, D, t([0, 3, 3, 10])).shape == (2, 3)

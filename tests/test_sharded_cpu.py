@@ -7,6 +7,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -74,4 +75,52 @@ def test_merge_two_ranks():
 
 
 def test_merge_short_shard_padded():
-    run([30, 500], k=50)  # rank 0 has fewer documents than k: padded with (-inf, max id)
+    run([30, 500], k=50)  # rank 0 has fewer documents than k: padded with (NaN, max id)
+
+
+def _faulty_worker(rank, world, port, mode, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+        dist.barrier()  # both ranks are up; the fault comes after this step
+    except Exception as e:
+        if rank == 0:
+            q.put(("setup failed: " + type(e).__name__, -1.0))
+        os._exit(0)
+    if rank == 1:  # leaves between steps, with no collective in flight
+        if mode == "stalls":
+            time.sleep(10)
+        os._exit(0)
+    from tilemaxsim_b200.sharded import merge_topk
+    v = torch.arange(20, dtype=torch.float32).view(2, 10)
+    i = torch.arange(20, dtype=torch.int64).view(2, 10)
+    t0 = time.monotonic()
+    try:
+        merge_topk(v, i, 10, group=dist.group.WORLD, topk_fn=oracle_topk)
+        q.put(("completed", time.monotonic() - t0))
+    except Exception as e:  # the failure reaches the host as an exception, not a hang
+        q.put((type(e).__name__, time.monotonic() - t0))
+    os._exit(0)  # no process-group teardown: it would wait for the missing rank
+
+
+@pytest.mark.parametrize("mode", ["dies", "stalls"])
+def test_missing_rank_fails_the_merge_within_the_timeout(mode):
+    """Failure detection on the host: a rank that exits (or stops responding) between search
+    steps makes the surviving rank's top-k merge raise within the process group's timeout."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_faulty_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        outcome, seconds = q.get(timeout=90)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert outcome != "completed" and not outcome.startswith("setup failed"), outcome
+    assert 0 <= seconds < 30

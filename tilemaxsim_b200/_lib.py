@@ -21,6 +21,7 @@ TMS_ERR_CUDA = 3
 TMS_ERR_TIMEOUT = 4
 TMS_ERR_WORKSPACE = 5
 TMS_ERR_TOO_LARGE = 6
+TMS_ERR_BAD_OFFSETS = 7
 
 TMS_F16, TMS_BF16, TMS_F32 = 0, 1, 2
 TMS_OUT_SCORE, TMS_OUT_TOKEN_MAX = 0, 1
@@ -35,6 +36,7 @@ SIGNATURES = {
     "tms_version": (ctypes.c_char_p, []),
     "tms_last_device_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint32)]),
     "tms_set_debug": (None, [_u64, _i32]),
+    "tms_validate_offsets": (_i32, [_vp, _i64, _i64, _vp]),
     "tms_dense_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i32]),
     "tms_dense_maxsim": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _i32,
                                 _vp, _sz, _vp]),

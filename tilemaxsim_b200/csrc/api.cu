@@ -4,6 +4,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "tms_device.cuh"
 #include "tms_internal.h"
 
 namespace tms {
@@ -113,6 +114,7 @@ extern "C" const char* tms_strerror(int code) {
     case TMS_ERR_TIMEOUT: return "device wait timed out";
     case TMS_ERR_WORKSPACE: return "workspace too small";
     case TMS_ERR_TOO_LARGE: return "problem exceeds the no-allocation entry point's static scratch";
+    case TMS_ERR_BAD_OFFSETS: return "document offsets negative, decreasing or past the token count";
     default: return "unknown error";
   }
 }
@@ -137,7 +139,37 @@ extern "C" int tms_last_device_error(void* stream, uint32_t* detail) {
       return TMS_ERR_CUDA;
   }
   if (detail) *detail = word;
-  return word ? TMS_ERR_TIMEOUT : TMS_OK;
+  if (word & kDevErrTimeout) return TMS_ERR_TIMEOUT;
+  return word ? TMS_ERR_BAD_OFFSETS : TMS_OK;
+}
+
+namespace tms {
+namespace {
+__global__ void validate_offsets_kernel(const int64_t* __restrict__ off, int64_t n_docs,
+                                        int64_t n_tokens, uint32_t* err) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i <= n_docs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t v = off[i];
+    const bool bad = v < 0 || v > n_tokens || (i > 0 && off[i - 1] > v);
+    if (bad) atomicCAS(err, 0u, kDevErrBadInput | static_cast<uint32_t>(i < 0x3fffffff ? i : 0x3fffffff));
+  }
+}
+}  // namespace
+}  // namespace tms
+
+extern "C" int tms_validate_offsets(const int64_t* doc_offsets, int64_t n_docs, int64_t n_tokens,
+                                    void* stream) {
+  if (n_docs < 0 || n_tokens < 0 || !doc_offsets) return TMS_ERR_INVALID;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  NvtxRange range("tms_validate_offsets");
+  const int64_t n = n_docs + 1;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  tms::validate_offsets_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      doc_offsets, n_docs, n_tokens, dev->err_word);
+  return cuda_status(cudaGetLastError());
 }
 
 // Test hook: wait limit for the bounded device waits (0 keeps the current value) and fault flags

@@ -1060,6 +1060,7 @@ extern "C" int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int
                                 const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
                                 float* out, int out_mode, void* workspace,
                                 size_t workspace_bytes, void* stream) {
+  NvtxRange nvtx_range("tms_dense_maxsim");
   if (dtype != TMS_F16 && dtype != TMS_BF16 && dtype != TMS_F32) return TMS_ERR_INVALID;
   if (out_mode != TMS_OUT_SCORE && out_mode != TMS_OUT_TOKEN_MAX) return TMS_ERR_INVALID;
   if (n_queries < 0 || nq < 0 || d <= 0 || n_docs < 0 || n_tokens < 0) return TMS_ERR_INVALID;
@@ -1307,6 +1308,7 @@ extern "C" int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_quer
                                         const int64_t* doc_offsets, int64_t n_docs,
                                         int64_t nd_uniform, float* out, int out_mode,
                                         void* stream) {
+  NvtxRange nvtx_range("tms_dense_maxsim_noalloc");
   // Nothing in the scratch has to start at zero: the pack kernel writes every byte of the query
   // tiles (padding included) and every partial sum is written before it is read.
   const size_t need = tms_dense_workspace_size(dtype, n_queries, nq, d, n_docs, out_mode);

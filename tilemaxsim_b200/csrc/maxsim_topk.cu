@@ -93,6 +93,7 @@ extern "C" int tms_dense_maxsim_topk(const void* Q, int dtype, int64_t n_queries
                                      int64_t nd_uniform, int64_t k, int64_t chunk_docs,
                                      int64_t id_base, float* out_vals, int64_t* out_ids,
                                      void* workspace, size_t workspace_bytes, void* stream) {
+  NvtxRange nvtx_range("tms_dense_maxsim_topk");
   if (n_queries < 0 || nq <= 0 || d <= 0 || n_docs < 0 || k < 0) return TMS_ERR_INVALID;
   if (n_queries == 0 || k == 0) return TMS_OK;
   if (k > n_docs || !out_vals || !out_ids) return TMS_ERR_INVALID;

@@ -192,6 +192,7 @@ using namespace tms;
 extern "C" int tms_pq_table(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
                             const void* codebook, int cb_dtype, int64_t M, int64_t K, int64_t dsub,
                             float* table, void* stream) {
+  NvtxRange nvtx_range("tms_pq_table");
   if (n_queries < 0 || nq < 0 || M <= 0 || K <= 0 || dsub <= 0) return TMS_ERR_INVALID;
   if (q_dtype < TMS_F16 || q_dtype > TMS_F32 || cb_dtype < TMS_F16 || cb_dtype > TMS_F32)
     return TMS_ERR_INVALID;
@@ -240,6 +241,7 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
                              const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
                              float* out, int mode, void* workspace, size_t workspace_bytes,
                              void* stream) {
+  NvtxRange nvtx_range("tms_pq_maxsim");
   if (mode != TMS_PQ_FAST && mode != TMS_PQ_EXACT) return TMS_ERR_INVALID;
   if (n_queries < 0 || nq <= 0 || M <= 0 || K <= 0 || dsub <= 0 || n_docs < 0 || n_tokens < 0)
     return TMS_ERR_INVALID;

@@ -12,6 +12,7 @@ namespace tms {
 // device error word: bit 31 = timeout, low bits = site id of the wait that gave up
 // ------------------------------------------------------------------------------------------------
 constexpr uint32_t kDevErrTimeout = 0x80000000u;
+constexpr uint32_t kDevErrBadInput = 0x40000000u;  // input validation (tms_validate_offsets)
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;

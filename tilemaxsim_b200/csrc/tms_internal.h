@@ -3,6 +3,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstddef>
 #include <cstdint>
 
@@ -35,6 +37,15 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, u
 long env_int(const char* name, long fallback);
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TMS_OK : TMS_ERR_CUDA; }
+
+// NVTX range around an entry point (named in Nsight Systems / Compute timelines; a no-op costing a
+// few nanoseconds when no tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

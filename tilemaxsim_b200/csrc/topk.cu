@@ -239,6 +239,7 @@ extern "C" size_t tms_topk_workspace_size(int64_t rows, int64_t n, int64_t k) {
 extern "C" int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, int64_t k,
                         const int64_t* ids_in, int64_t ld_ids, int64_t id_base, float* out_vals,
                         int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream) {
+  NvtxRange nvtx_range("tms_topk");
   if (rows < 0 || n < 0 || k < 0 || ld < n) return TMS_ERR_INVALID;
   if (rows == 0 || k == 0) return TMS_OK;
   if (k > n || !scores || !out_vals || !out_ids) return TMS_ERR_INVALID;

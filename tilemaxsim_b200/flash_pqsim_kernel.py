@@ -20,6 +20,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .maxsim import _check_offsets_enabled, validate_offsets
 
 
 def _codes_u8(codes: torch.Tensor) -> torch.Tensor:
@@ -88,6 +89,8 @@ class TileMaxSimPQ:
         if not self.exact and Qb.dtype != torch.float16 and self._tensor_shape():
             Qb = Qb.half()  # the tensor-core path multiplies fp16 queries (fast-mode tolerance)
         codes_tokens = _codes_u8(codes_tokens)
+        if offsets is not None and _check_offsets_enabled():
+            validate_offsets(offsets, codes_tokens.shape[0])
         with torch.cuda.device(dev):
             out = torch.empty(Bq, n_docs, dtype=torch.float32, device=dev)
             if Bq == 0 or n_docs == 0:

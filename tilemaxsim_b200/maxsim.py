@@ -8,10 +8,36 @@ per-query top-k (the reference ranks with ``torch.topk``, src/cycle3_experiments
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
 from . import _lib
+
+
+def validate_offsets(doc_offsets: torch.Tensor, n_tokens: int) -> None:
+    """Checks a document offsets array on its GPU (tms_validate_offsets): every entry in
+    [0, n_tokens] and the array non-decreasing. Raises ValueError naming a bad index. Synchronises
+    the current stream. The scoring calls never read outside their arrays whatever the offsets;
+    this only tells a caller that its offsets are malformed. Setting TMS_CHECK_OFFSETS=1 runs it
+    before every ragged scoring call."""
+    lib = _lib.load()
+    dev = _lib.require_cuda(doc_offsets)
+    off = _as_contig(doc_offsets.to(torch.int64))
+    with torch.cuda.device(dev):
+        rc = lib.tms_validate_offsets(ctypes.c_void_p(off.data_ptr()), off.numel() - 1, int(n_tokens),
+                                      ctypes.c_void_p(_lib.stream_handle(dev)))
+        _lib.check(rc, "tms_validate_offsets")
+        status, word = _lib.last_device_error(dev)
+    if status == _lib.TMS_ERR_BAD_OFFSETS:
+        raise ValueError(f"doc_offsets[{word & 0x3FFFFFFF}] is negative, smaller than the entry before "
+                         f"it, or past n_tokens={n_tokens}")
+    if status != _lib.TMS_OK:
+        raise _lib.TileMaxSimError(status, "device error word")
+
+
+def _check_offsets_enabled() -> bool:
+    return os.environ.get("TMS_CHECK_OFFSETS", "0") not in ("", "0")
 
 
 def _as_contig(t: torch.Tensor) -> torch.Tensor:
@@ -39,6 +65,8 @@ def _dense_call(Qb: torch.Tensor, D_tokens: torch.Tensor, doc_offsets: torch.Ten
         if doc_offsets.dtype != torch.int64:
             doc_offsets = doc_offsets.to(torch.int64)
         doc_offsets = _as_contig(doc_offsets)
+        if _check_offsets_enabled():
+            validate_offsets(doc_offsets, D_tokens.shape[0])
     dt = _lib.DTYPE_CODE[D_tokens.dtype]
     shape = (Bq, n_docs) if out_mode == _lib.TMS_OUT_SCORE else (Bq, n_docs, Nq)
     with torch.cuda.device(dev):
