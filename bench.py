@@ -239,6 +239,13 @@ def config_dict(args, cfg) -> dict:
                   else "corpus fits in L2"}
 
 
+def percentiles(xs: list[float]) -> list[float]:
+    """[p50, p95] of per-launch kernel times (this rank's, CUDA events)."""
+    ys = sorted(xs)
+    pick = lambda q: ys[min(len(ys) - 1, int(round(q * (len(ys) - 1))))]  # noqa: E731
+    return [pick(0.5), pick(0.95)]
+
+
 def topk_launches(rows: int, n: int, k: int) -> int:
     """Kernels one tms_topk call launches (csrc/topk.cu: one sort for n <= 16384, else a slice
     select, plus a merge sort when the row is split into several slices)."""
@@ -311,7 +318,8 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
         end.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(end) / args.steps
-    kern_ms = sum(a.elapsed_time(b) for a, b in score_ev) / len(score_ev)
+    kern_list = [a.elapsed_time(b) for a, b in score_ev]
+    kern_ms = sum(kern_list) / len(kern_list)
     if world == 1:  # the captured step (see run_ours)
         from tilemaxsim_b200 import GraphedStep
         def plain_step(Q):  # the search step without the timing events
@@ -359,6 +367,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
                                f"uint8 codes per GPU (M={M}, K={K}, dsub={dsub}, fp32 codebook), top-{k}",
                    "l2": "codes larger than L2"},
         "queries_per_s": nqry / (ms * 1e-3), "pq_kernel_ms": kern_ms,
+        "pq_kernel_ms_p50_p95": percentiles(kern_list),
         "lut_lookups_per_s": lookups / (kern_ms * 1e-3),
         # default path: codes decoded in shared memory, MMA on the tensor cores, the epilogue reading
         # every fp32 similarity from TMEM (B_q*Nq*T values) -- the same bound as the dense kernel
@@ -420,7 +429,8 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end) / args.steps
-    dense_ms = sum(a.elapsed_time(b) for a, b in dense_ev) / len(dense_ev)
+    dense_list = [a.elapsed_time(b) for a, b in dense_ev]
+    dense_ms = sum(dense_list) / len(dense_list)
 
     # e2e: public API with host queries in pinned memory and results copied back, every step. On
     # one GPU the step is the captured graph (tilemaxsim_b200.GraphedStep); across GPUs the step
@@ -489,6 +499,7 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "queries_per_s": nqry / (ms * 1e-3),
         "corpus_tokens_per_s": T_total / (ms * 1e-3),
         "dense_kernel_ms": dense_ms,
+        "dense_kernel_ms_p50_p95": percentiles(dense_list),
         "dense_hbm_gbs": bytes_launch / (dense_ms * 1e-3) / 1e9,
         "dense_tflops": flops_launch / (dense_ms * 1e-3) / 1e12,
         "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": ach, "peak": peak, "unit": unit,
