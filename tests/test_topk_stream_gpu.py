@@ -37,6 +37,20 @@ def test_streamed_topk_equals_full_matrix_topk(bq, k, chunk, cuda_device):
     assert torch.equal(got_i, want_i)
 
 
+@pytest.mark.parametrize("nq,dtype", [(40, torch.float16), (32, torch.bfloat16), (100, torch.bfloat16)])
+def test_streamed_topk_long_queries_and_bf16(nq, dtype, cuda_device):
+    """Queries longer than 32 tokens (per-chunk partial sums inside every document chunk) and
+    bf16 inputs, chunked, against the full-matrix top-k."""
+    from tilemaxsim_b200 import maxsim_batched, maxsim_topk, topk
+    D, off = _corpus(1500, 7, cuda_device)
+    D = D.to(dtype)
+    Qb = R.normalized((3, nq, 128), 8).to(dtype).to(cuda_device)
+    want_v, want_i = topk(maxsim_batched(Qb, D, off), 64)
+    got_v, got_i = maxsim_topk(Qb, D, off, 64, chunk_docs=211)
+    torch.testing.assert_close(got_v, want_v, rtol=0, atol=0)
+    assert torch.equal(got_i, want_i)
+
+
 def test_streamed_topk_uniform_documents_c_abi(cuda_device):
     """The uniform-length layout (no offsets array) through the C ABI, chunked."""
     from tilemaxsim_b200 import _lib, maxsim_padded, topk
