@@ -187,14 +187,14 @@ def run_reference(args, cfg, rank: int) -> None:
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     sample = (f"per step 1 query x {n_s} ragged docs ({int(off[-1])} tokens, d={d}) + top-{min(k, n_s)}, "
               "NumPy fp32 restatement of the reference's pytorch_maxsim_naive on all host cores")
-    print(json.dumps({
+    emit_json({
         "impl": "reference", "metric": "doc-tokens scored/s", "value": val, "unit": "doc-tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args, cfg),
         "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": "doc-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "gpu_launches": 0}))
+        "gpu_launches": 0})
 
 
 def run_reference_pq(args, cfg, rank: int) -> None:
@@ -218,7 +218,7 @@ def run_reference_pq(args, cfg, rank: int) -> None:
     dt = (time.perf_counter() - t0) / args.steps
     val = n_s * nd / dt
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    print(json.dumps({
+    emit_json({
         "impl": "reference", "metric": "doc-tokens scored/s", "value": val, "unit": "doc-tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
@@ -226,7 +226,7 @@ def run_reference_pq(args, cfg, rank: int) -> None:
         "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": cores, "kind": "port",
                          "sample": f"per step 1 query x {n_s} docs x {nd} codes, NumPy ADC restatement"},
         "e2e": {"value": val, "unit": "doc-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "gpu_launches": 0}))
+        "gpu_launches": 0})
 
 
 def config_dict(args, cfg) -> dict:
@@ -237,6 +237,26 @@ def config_dict(args, cfg) -> dict:
             "parallelism": f"corpus-sharded x{args.gpus}, NCCL all-gather of per-shard top-k",
             "l2": "inputs larger than L2 (corpus >> 126 MB)" if n_docs * (lo + hi) / 2 * d * 2 > 126e6
                   else "corpus fits in L2"}
+
+
+# The JSON result line goes to the process's real standard output; everything libraries print on
+# file descriptor 1 while the benchmark runs (NCCL's version banner, for one) is sent to standard
+# error, so standard output carries exactly one line per run.
+_RESULT_FD: int | None = None
+
+
+def route_library_output_to_stderr() -> None:
+    global _RESULT_FD
+    if _RESULT_FD is None:
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit_json(obj: dict) -> None:
+    line = (json.dumps(obj) + "\n").encode()
+    sys.stdout.flush()
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, line)
 
 
 def percentiles(xs: list[float]) -> list[float]:
@@ -359,7 +379,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
     gather_bytes = float(T) * M * dsub * 2
     smem_peak = 128.0 * torch.cuda.get_device_properties(device).multi_processor_count * \
         (ClockSampler.last_sm_mhz or 1965.0) * 1e6 / 1e9
-    print(json.dumps({
+    emit_json({
         "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
@@ -385,7 +405,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s", "h2d_bytes_per_step": Qh.numel() * 2,
                 "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
         "gpu_launches": search_launches(nqry, n_docs, k, world, pq_score_launches(nqry, nq, M, K, dsub)) * args.steps,
-        "clocks": clocks}), flush=True)
+        "clocks": clocks})
 
 
 def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
@@ -518,7 +538,7 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     }
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg)
-    print(json.dumps(out), flush=True)
+    emit_json(out)
 
 
 def main() -> int:
@@ -530,6 +550,7 @@ def main() -> int:
     ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PQ_CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    route_library_output_to_stderr()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS.get(args.config) or PQ_CONFIGS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -53,3 +53,23 @@ def test_reference_baselines_run_on_cpu():
     p = R.pq_case()
     np.testing.assert_allclose(pytorch_pqsim_baseline(p["Q"], p["codebook"], p["codes"]).numpy(),
                                O.pq_maxsim_decompress(p["Q"], p["codebook"], p["codes"]), rtol=1e-5, atol=1e-4)
+
+
+def test_bench_reference_arm_prints_one_json_line():
+    """The reference arm runs on host cores: `bench.py --impl reference` prints exactly one JSON
+    line on standard output with the contract's keys (anything a library prints goes to stderr)."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--config", "c1",
+                        "--steps", "1", "--warmup", "1"], capture_output=True, text=True, cwd=root, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["value"] > 0 and d["e2e"]["h2d_bytes_per_step"] == 0
