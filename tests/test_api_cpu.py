@@ -73,3 +73,14 @@ def test_bench_reference_arm_prints_one_json_line():
                 "higher_is_better", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["value"] > 0 and d["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_graphed_step_needs_device_inputs():
+    """GraphedStep captures GPU work only: CPU example inputs are refused before any capture."""
+    import pytest
+    import torch
+    from tilemaxsim_b200 import GraphedStep
+    with pytest.raises(ValueError):
+        GraphedStep(lambda q: q, torch.zeros(2, 32, 128))
+    with pytest.raises(ValueError):
+        GraphedStep(lambda: None)
