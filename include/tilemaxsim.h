@@ -158,6 +158,27 @@ TMS_API int tms_dense_maxsim_topk(const void* Q, int dtype, int64_t n_queries, i
                                   int64_t* out_ids, void* workspace, size_t workspace_bytes,
                                   void* stream);
 
+/* ---------------------------------------------------------------- residual-compressed corpora */
+
+/* Workspace for tms_residual_maxsim (0 = unsupported shape: d must be 64 or 128). */
+TMS_API size_t tms_residual_workspace_size(int64_t n_queries, int64_t nq, int64_t d, int64_t n_docs);
+
+/* MaxSim over a corpus stored as ColBERTv2-style residual codes: token t is
+ *   x = centroids[codes[t], :] + bucket_weights[b_j]   (j = 0..d-1),
+ * optionally scaled to unit length (normalize != 0), where b_j is dimension j's nbits-bit bucket
+ * index: bit k of b_j is bit (j*nbits + k) of the token's residual row, bits numbered from the most
+ * significant bit of byte 0 (residuals: n_tokens x d*nbits/8 bytes; nbits 1, 2 or 4). Tokens are
+ * decoded on chip, rounded once to fp16 and scored like tms_dense_maxsim (fp16 queries, fp32
+ * accumulation; offsets or nd_uniform as there): out[q * n_docs + doc]. centroids: (n_centroids, d)
+ * fp16, 16-byte aligned; codes int32 (clamped to [0, n_centroids)); bucket_weights: 2^nbits fp32.
+ * d = 64 or 128. The workspace must be 1024-byte aligned. */
+TMS_API int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,
+                                const void* centroids, int64_t n_centroids, const int32_t* codes,
+                                const uint8_t* residuals, const float* bucket_weights, int nbits,
+                                int normalize, int64_t n_tokens, const int64_t* doc_offsets,
+                                int64_t n_docs, int64_t nd_uniform, float* out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- top-k */
 
 TMS_API size_t tms_topk_workspace_size(int64_t rows, int64_t n, int64_t k);

@@ -81,3 +81,21 @@ def test_segment_max_ignores_rows_past_the_last_document():
     table[:, :, 1] = 100.0
     tok = O.pq_token_scores(table, codes)
     np.testing.assert_array_equal(O._segment_max(tok, np.array([0, 5, 10]), 0).ravel(), [0, 0])
+
+
+def test_residual_decompress_bit_order():
+    """Known answer for the residual layout: one 8-dimension token, nbits = 2, residual bytes
+    0b00011011 and 0b11100100. MSB-first pairs give fields 00,01,10,11 / 11,10,01,00; bit k of a
+    dimension's index is its pair's k-th bit, so the indices are 0,2,1,3 / 3,1,2,0."""
+    centroids = np.zeros((2, 8), np.float16)
+    centroids[1] = np.arange(8, dtype=np.float16)
+    bw = np.array([-1.0, -0.25, 0.25, 1.0], np.float32)
+    R = np.array([[0b00011011, 0b11100100]], np.uint8)
+    got = O.residual_decompress(centroids, np.array([1]), R, bw, 2, normalize=False)
+    idx = np.array([0, 2, 1, 3, 3, 1, 2, 0])
+    np.testing.assert_array_equal(got[0], (np.arange(8) + bw[idx]).astype(np.float16))
+    unit = O.residual_decompress(centroids, np.array([1]), R, bw, 2, normalize=True).astype(np.float32)
+    np.testing.assert_allclose(np.linalg.norm(unit[0]), 1.0, rtol=2e-3)
+    one = O.residual_decompress(np.zeros((1, 8), np.float16), np.array([0]), np.array([[0b10000000]], np.uint8),
+                                np.array([0.0, 1.0], np.float32), 1, normalize=False)
+    np.testing.assert_array_equal(one[0], np.array([1, 0, 0, 0, 0, 0, 0, 0], np.float16))

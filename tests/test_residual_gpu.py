@@ -1,0 +1,62 @@
+"""Residual-compressed corpora (ColBERTv2 layout): tokens decoded on chip by the dense kernel's
+decoder warps and scored on the tensor cores, against the oracle's decompress-then-score."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import recipes as R
+from oracle import maxsim_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _corpus(d, nbits, seed, n_docs=400, hi=150, n_cent=1000):
+    g = R.gen(seed)
+    cent = torch.nn.functional.normalize(torch.randn(n_cent, d, generator=g), dim=-1).half()
+    lens = R.ragged_lengths(n_docs, 0, hi, seed)
+    lens[::97] = 0  # a few empty documents in every corpus
+    off = R.offsets_from_lengths(lens)
+    T = int(off[-1])
+    codes = torch.randint(0, n_cent, (T,), generator=g, dtype=torch.int32)
+    res = torch.randint(0, 256, (T, d * nbits // 8), generator=g, dtype=torch.uint8)
+    bw = torch.sort(torch.randn(1 << nbits, generator=g) * 0.05).values
+    return cent, codes, res, bw, off
+
+
+@pytest.mark.parametrize("nqry,nq,nbits,normalize,d", [
+    (1, 32, 2, True, 128), (5, 32, 2, True, 128), (3, 32, 1, False, 128), (2, 32, 4, True, 128),
+    (1, 40, 2, True, 128), (1, 32, 2, True, 64), (6, 20, 4, False, 64)])
+def test_residual_vs_oracle(nqry, nq, nbits, normalize, d, cuda_device):
+    from tilemaxsim_b200 import ResidualMaxSim
+    cent, codes, res, bw, off = _corpus(d, nbits, seed=nqry + 10 * nbits + d)
+    Q = R.normalized((nqry, nq, d), 7)
+    scorer = ResidualMaxSim(cent.to(cuda_device), bw.to(cuda_device), nbits, normalize)
+    got = scorer.score_queries(Q.to(cuda_device), codes.to(cuda_device), res.to(cuda_device),
+                               torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    D = O.residual_decompress(cent, codes, res, bw, nbits, normalize)
+    want = O.maxsim_ragged(Q, torch.from_numpy(D), off)
+    inf = np.isinf(want)
+    assert inf.any()  # empty documents are in the corpus
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)
+
+
+def test_residual_empty_corpus_and_code_clamp(cuda_device):
+    """A corpus of empty documents scores -inf; centroid ids out of range are clamped, never read
+    outside the centroid table."""
+    from tilemaxsim_b200 import ResidualMaxSim
+    cent, codes, res, bw, off = _corpus(128, 2, seed=3, n_docs=50)
+    scorer = ResidualMaxSim(cent.to(cuda_device), bw.to(cuda_device), 2)
+    Q = R.normalized((2, 32, 128), 8).to(cuda_device)
+    empty = scorer.score_queries(Q, codes[:0].to(cuda_device), res[:0].to(cuda_device),
+                                 torch.zeros(6, dtype=torch.int64, device=cuda_device))
+    assert empty.shape == (2, 5) and torch.all(torch.isneginf(empty))
+    wild = codes.clone()
+    wild[::7] = 10**6
+    wild[1::7] = -5
+    got = scorer.score_queries(Q, wild.to(cuda_device), res.to(cuda_device), torch.from_numpy(off).to(cuda_device))
+    want = O.maxsim_ragged(Q.cpu(), torch.from_numpy(O.residual_decompress(cent, wild, res, bw, 2)), off)
+    inf = np.isinf(want)
+    np.testing.assert_allclose(got.cpu().numpy()[~inf], want[~inf], rtol=1e-3, atol=1e-3)

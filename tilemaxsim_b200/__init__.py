@@ -14,11 +14,12 @@ from .flash_maxsim_v2 import flash_maxsim_v2, flash_maxsim_v2_multiquery
 from .flash_pqsim_kernel import TileMaxSimPQ, pytorch_pqsim_baseline
 from .graphed import GraphedStep
 from .maxsim import maxsim_batched, maxsim_padded, maxsim_topk, topk, validate_offsets
+from .residual import ResidualMaxSim
 
 __version__ = "0.1.0"
 __all__ = [
     "flash_maxsim_single", "flash_maxsim_batch", "flash_maxsim_multi_doc", "flash_maxsim_token_max",
     "pytorch_maxsim_naive", "pytorch_maxsim_loop", "flash_maxsim_v2", "flash_maxsim_v2_multiquery",
     "TileMaxSimPQ", "pytorch_pqsim_baseline", "maxsim_batched", "maxsim_padded", "maxsim_topk", "topk",
-    "GraphedStep", "validate_offsets",
+    "GraphedStep", "validate_offsets", "ResidualMaxSim",
 ]

@@ -51,6 +51,9 @@ SIGNATURES = {
     "tms_dense_topk_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i64, _i64]),
     "tms_dense_maxsim_topk": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64,
                                      _i64, _vp, _vp, _vp, _sz, _vp]),
+    "tms_residual_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "tms_residual_maxsim": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i64, _vp, _i64,
+                                   _i64, _vp, _vp, _sz, _vp]),
     "tms_topk_workspace_size": (_sz, [_i64, _i64, _i64]),
     "tms_topk": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _sz, _vp]),
 }

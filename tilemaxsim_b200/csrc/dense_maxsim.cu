@@ -77,6 +77,16 @@ struct DenseArgs {
   const void* codebook;
   int cb_dtype, pq_M, pq_K, pq_dsub;
   uint32_t cb_bytes;   // fp16 codebook bytes staged in shared memory (0 for the dense kernel)
+  // Residual-compressed tokens (the PQ variant's decoders in residual mode, res_nbits != 0):
+  // token = centroids[res_codes[t]] + bucket_weights[per-dimension nbits index from res_bits],
+  // optionally L2-normalised; the fp32 bucket weights take the codebook's shared-memory slot.
+  const __half* res_centroids;  // (res_ncent, d) fp16
+  const int32_t* res_codes;     // (n_tokens,)
+  const uint8_t* res_bits;      // (n_tokens, d * res_nbits / 8)
+  const float* res_bw;          // (1 << res_nbits,)
+  int64_t res_ncent;
+  int res_nbits;      // 0: PQ mode; 1, 2 or 4: residual mode
+  int res_normalize;
   int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits);
                        // bits 2/3: skip the epilogue math / the MMAs (timing experiments only)
 };
@@ -155,7 +165,120 @@ __device__ __forceinline__ float range_max32(float acc, const uint32_t (&r)[32],
   return fmaxf(m0, m1);
 }
 
-template <int TN, bool QRES, bool TF32, bool PQ>
+// One residual-compressed token row (d <= 128 values) rebuilt into a swizzled stage row:
+// value j = centroid[j] + bwr[nbits-wide field of residual byte j / (8 / NB)], optionally scaled
+// to unit length (a first pass over the values gives the norm), rounded once to fp16. Each
+// 16-byte unit (8 dimensions) pairs with its NB residual bytes, read as one little-endian
+// integer, so every shift is a compile-time constant.
+template <int NB>
+__device__ __forceinline__ uint32_t residual_unit_bits(const uint8_t* rrow, int u) {
+  if (NB == 4) return __ldg(reinterpret_cast<const uint32_t*>(rrow) + u);
+  if (NB == 2) return __ldg(reinterpret_cast<const unsigned short*>(rrow) + u);
+  return __ldg(rrow + u);
+}
+template <int NB>
+__device__ __forceinline__ float residual_value(const uint4& c, uint32_t bits, const float* bwr, int e) {
+  constexpr int kPerByte = 8 / NB;
+  constexpr uint32_t kMask = (1u << NB) - 1u;
+  const uint32_t cw = (e < 2) ? c.x : (e < 4) ? c.y : (e < 6) ? c.z : c.w;
+  const float cv = __half2float(__ushort_as_half(static_cast<unsigned short>((e & 1) ? (cw >> 16) : (cw & 0xffffu))));
+  const int lb = e / kPerByte, q = e % kPerByte;  // byte within the unit's bits, field within it
+  return cv + bwr[(bits >> (8 * lb + 8 - NB * (q + 1))) & kMask];
+}
+// A quarter of one token (dimensions [d/4 * h, d/4 * (h + 1)): `upp` = d / 32 units of 8), held
+// by one of the four decoder threads that share the token.
+struct ResPart {
+  uint4 c[4];       // centroid units
+  uint32_t b[4];    // each unit's residual bits
+};
+template <int NB>
+__device__ __forceinline__ void res_part_load(ResPart& P, const uint4* crow, const uint8_t* rrow,
+                                              int u0, int upp, bool valid) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool on = valid && i < upp;
+    P.c[i] = on ? __ldg(crow + u0 + i) : make_uint4(0, 0, 0, 0);
+    P.b[i] = on ? residual_unit_bits<NB>(rrow, u0 + i) : 0u;
+  }
+}
+// Values of the part, scaled by the token's norm (a sum over the four threads of the token, lanes
+// 4k..4k+3), rounded to fp16 and stored in the swizzled stage row. Every lane of the warp calls it.
+template <int NB, int TN>
+__device__ __forceinline__ void res_part_store(const ResPart& P, const float* bwr, int u0, int upp,
+                                               bool normalize, bool valid, uint8_t* rowp, uint32_t sw) {
+  float scale = 1.0f;
+  if (normalize) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i >= upp) break;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float x = residual_value<NB>(P.c[i], P.b[i], bwr, e);
+        ss = fmaf(x, x, ss);
+      }
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    scale = ss > 0.0f ? rsqrtf(ss) : 0.0f;
+  }
+  if (!valid) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i >= upp) break;
+    const int u = u0 + i;
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const __half2 h = __floats2half2_rn(residual_value<NB>(P.c[i], P.b[i], bwr, e) * scale,
+                                          residual_value<NB>(P.c[i], P.b[i], bwr, e + 1) * scale);
+      pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(rowp + (u >> 3) * (TN * 128) + (((static_cast<uint32_t>(u) & 7u) ^ sw) << 4)) =
+        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+// One tile (TN = 128 tokens) decoded by 128 threads: thread dt holds part dt % 4 of token
+// 32 p + dt / 4 in pass p (4 passes); the next pass's loads are issued before this pass's math.
+template <int NB, int TN>
+__device__ __forceinline__ void decode_residual_tile(const int32_t (&code)[4], int64_t t0, int64_t tok_hi,
+                                                     int dt, int d, const __half* cent, int64_t ncent,
+                                                     const uint8_t* res_bits, const float* bwr,
+                                                     bool normalize, uint8_t* stage) {
+  const int tk = dt >> 2, h = dt & 3;
+  const int upp = d / 32, u0 = h * upp;
+  const int64_t rbytes = static_cast<int64_t>(d) * NB / 8;
+  auto src = [&](int p, const uint4*& crow, const uint8_t*& rrow) -> bool {
+    const int64_t tok = t0 + 32 * p + tk;
+    const bool v = tok < tok_hi;
+    int32_t c = code[p];
+    c = c < 0 ? 0 : (c >= ncent ? static_cast<int32_t>(ncent - 1) : c);  // never outside the table
+    crow = reinterpret_cast<const uint4*>(cent + static_cast<int64_t>(c) * d);
+    rrow = res_bits + (v ? tok : 0) * rbytes;
+    return v;
+  };
+  ResPart cur, nxt;
+  const uint4* crow;
+  const uint8_t* rrow;
+  bool v_cur = src(0, crow, rrow);
+  res_part_load<NB>(cur, crow, rrow, u0, upp, v_cur);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    bool v_nxt = false;
+    if (p + 1 < 4) {
+      v_nxt = src(p + 1, crow, rrow);
+      res_part_load<NB>(nxt, crow, rrow, u0, upp, v_nxt);
+    }
+    const int r = 32 * p + tk;
+    res_part_store<NB, TN>(cur, bwr, u0, upp, normalize, v_cur, stage + r * 128, static_cast<uint32_t>(r & 7));
+    if (p + 1 < 4) {
+      cur = nxt;
+      v_cur = v_nxt;
+    }
+  }
+}
+
+template <int TN, bool QRES, bool TF32, bool PQ, bool RES = false>
 __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
@@ -233,7 +356,16 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
   }
   if (PQ) {  // stage the codebook in shared memory as fp16 (every thread helps)
     __half* cbs = reinterpret_cast<__half*>(smem + L.cb_off);
-    const int n = a.pq_M * a.pq_K * a.pq_dsub;
+    if (a.res_nbits) {
+      // entry v = the weight of the bucket whose index is v's nbits bits reversed: the packing
+      // puts a dimension's lowest index bit first (highest in its byte field), so a field read
+      // as a plain number indexes this table directly
+      float* bws = reinterpret_cast<float*>(smem + L.cb_off);
+      const int nb = a.res_nbits;
+      for (int v = threadIdx.x; v < (1 << nb); v += blockDim.x)
+        bws[v] = a.res_bw[__brev(static_cast<unsigned>(v)) >> (32 - nb)];
+    }
+    const int n = a.res_nbits ? 0 : a.pq_M * a.pq_K * a.pq_dsub;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       float v;
       if (a.cb_dtype == TMS_F16) v = __half2float(reinterpret_cast<const __half*>(a.codebook)[i]);
@@ -298,7 +430,53 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
         }
       }
     }
-  } else if (PQ && warp >= kDecodeWarp0) {
+  } else if (PQ && RES && warp >= kDecodeWarp0) {
+    // ------------------------------------------------------------------ residual decoders
+    // Row r of a D stage = token t0 + r: centroids[code] + bucket_weights[index of each dimension]
+    // (optionally scaled to unit length), rounded once to fp16, written in the 128-byte-swizzle
+    // layout (unit u of row r at u ^ (r % 8)). Four threads share a token (a quarter of its d <= 128
+    // dimensions each). A dimension's index is the nbits-wide field of its residual byte
+    // (MSB-first packing), looked up in the bit-reversed weight table staged above.
+    const float* bwr = reinterpret_cast<const float*>(smem + L.cb_off);
+    const int dt = threadIdx.x - kDecodeWarp0 * 32;  // 0..127
+    const int d = a.kc * 64;
+    const int nb = a.res_nbits;
+    const int64_t ncent = a.res_ncent;
+    const bool nrm = a.res_normalize != 0;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = !(a.debug_flags & 1);
+    // the centroid ids of the next tile's four passes are loaded while this tile is decoded
+    int32_t code_n[4];
+    auto load_codes = [&](int64_t t0) {
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int64_t tok = t0 + 32 * p + (dt >> 2);
+        code_n[p] = tok < tok_hi ? __ldg(a.res_codes + tok) : 0;
+      }
+    };
+    load_codes(tok_lo);
+    for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
+      int32_t code[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) code[p] = code_n[p];
+      load_codes(t0 + TN);
+      int w = 0;
+      if (lane == 0) w = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 10);
+      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+      uint8_t* stage = smem + L.stage_off + static_cast<size_t>(s) * L.stage_bytes;
+      if (nb == 2)
+        decode_residual_tile<2, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
+      else if (nb == 1)
+        decode_residual_tile<1, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
+      else
+        decode_residual_tile<4, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full_bar(s));
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+  } else if (PQ && !RES && warp >= kDecodeWarp0) {
     // ------------------------------------------------------------------ PQ decoders
     // Row r of a D stage = token t0 + r rebuilt from its M codes: codebook row (m, code) is
     // dsub fp16 values = dsub/8 16-byte units, placed at columns m*dsub.. of the row in the
@@ -1010,10 +1188,10 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   return TMS_OK;
 }
 
-template <int TN, bool QRES, bool TF32, bool PQ = false>
+template <int TN, bool QRES, bool TF32, bool PQ = false, bool RES = false>
 int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
                    const DensePlan& p, cudaStream_t st) {
-  auto kern = dense_maxsim_kernel<TN, QRES, TF32, PQ>;
+  auto kern = dense_maxsim_kernel<TN, QRES, TF32, PQ, RES>;
   const SmemLayout L = dense_smem_layout(TN, QRES, p.G, p.kc, p.stages, p.n_mtiles == 1,
                                          p.cb_bytes);
   cudaError_t e =
@@ -1191,20 +1369,21 @@ size_t pq_mma_workspace_size(int64_t n_queries, int64_t nq, int64_t d, int64_t n
   return tms_dense_workspace_size(TMS_F16, n_queries, nq, d, n_docs, TMS_OUT_SCORE);
 }
 
-int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook, int cb_dtype,
-                  int64_t M, int64_t K, int64_t dsub, const uint8_t* codes, int64_t n_tokens,
-                  const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
-                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
-  const size_t cb_bytes = pq_mma_codebook_bytes(M, K, dsub);
-  if (!cb_bytes || n_tokens <= 0 || n_tokens >= (int64_t(1) << 31)) return TMS_ERR_UNSUPPORTED;
+// The dense kernel with decoder warps (PQ codes or residual-compressed tokens): query packing,
+// the Q tensor map, the launch, and the chunk sum for Nq > 32. `fill` sets the decoder's fields
+// of the argument block.
+template <bool RES, typename Fill>
+int decoder_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d, uint32_t cb_bytes,
+                   int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform,
+                   float* out, void* workspace, size_t workspace_bytes, cudaStream_t st, Fill fill) {
+  if (n_tokens <= 0 || n_tokens >= (int64_t(1) << 31)) return TMS_ERR_UNSUPPORTED;
   if (reinterpret_cast<uintptr_t>(Q) & 15) return TMS_ERR_UNSUPPORTED;
   int status = TMS_OK;
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
-  const int64_t d = M * dsub;
   DensePlan p;
   int rc = plan_dense(TMS_F16, n_queries, nq, d, n_docs, n_tokens, TMS_OUT_SCORE, dev->num_sms,
-                      dev->max_smem_optin, &p, static_cast<uint32_t>(cb_bytes),
+                      dev->max_smem_optin, &p, cb_bytes,
                       /* 128-token tiles: two query tiles per CTA fit beside the codebook */ 128);
   if (rc != TMS_OK) return rc;
   if (!workspace || workspace_bytes < p.qp_bytes + p.partial_bytes) return TMS_ERR_WORKSPACE;
@@ -1225,7 +1404,7 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
   rc = encode_tmap_2d(&qm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qp, static_cast<uint64_t>(d),
                       static_cast<uint64_t>(p.n_mtiles) * kQTileRows, row_bytes, p.cw, kQTileRows);
   if (rc != TMS_OK) return rc;
-  DenseArgs args;
+  DenseArgs args = {};
   args.docs.offsets = doc_offsets;
   args.docs.n_docs = n_docs;
   args.docs.nd = doc_offsets ? 0 : nd_uniform;
@@ -1243,23 +1422,38 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
   args.stages = p.stages;
   args.out_mode = TMS_OUT_SCORE;
   args.ab_format = 0u;
-  args.codes = codes;
   args.n_code_rows = n_tokens;
-  args.codebook = codebook;
-  args.cb_dtype = cb_dtype;
-  args.pq_M = static_cast<int>(M);
-  args.pq_K = static_cast<int>(K);
-  args.pq_dsub = static_cast<int>(dsub);
-  args.cb_bytes = static_cast<uint32_t>(cb_bytes);
+  args.cb_bytes = cb_bytes;
   args.debug_flags = debug_flags();
-  rc = (p.TN == 256) ? launch_dense_t<256, true, false, true>(qm, qm, args, p, st)
-                     : launch_dense_t<128, true, false, true>(qm, qm, args, p, st);
+  fill(args);
+  if (p.TN == 256)
+    rc = launch_dense_t<256, true, false, true, RES>(qm, qm, args, p, st);
+  else
+    rc = launch_dense_t<128, true, false, true, RES>(qm, qm, args, p, st);
   if (rc != TMS_OK || p.nchunk == 1) return rc;
   const int64_t total = n_queries * n_docs;
   blocks = static_cast<int>((total + 255) / 256);
   if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
   sum_query_chunks_kernel<<<blocks, 256, 0, st>>>(partial, out, n_queries, n_docs, p.nchunk);
   return cuda_status(cudaGetLastError());
+}
+
+int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook, int cb_dtype,
+                  int64_t M, int64_t K, int64_t dsub, const uint8_t* codes, int64_t n_tokens,
+                  const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
+                  void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const size_t cb_bytes = pq_mma_codebook_bytes(M, K, dsub);
+  if (!cb_bytes) return TMS_ERR_UNSUPPORTED;
+  return decoder_maxsim<false>(Q, n_queries, nq, M * dsub, static_cast<uint32_t>(cb_bytes), n_tokens,
+                               doc_offsets, n_docs, nd_uniform, out, workspace, workspace_bytes, st,
+                               [&](DenseArgs& a) {
+                                 a.codes = codes;
+                                 a.codebook = codebook;
+                                 a.cb_dtype = cb_dtype;
+                                 a.pq_M = static_cast<int>(M);
+                                 a.pq_K = static_cast<int>(K);
+                                 a.pq_dsub = static_cast<int>(dsub);
+                               });
 }
 
 }  // namespace tms
@@ -1318,4 +1512,56 @@ extern "C" int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_quer
   if (rc != TMS_OK) return rc;
   return tms_dense_maxsim(Q, dtype, n_queries, nq, d, D, n_tokens, doc_offsets, n_docs, nd_uniform,
                           out, out_mode, scratch, kNoAllocScratchBytes, stream);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Residual-compressed corpora: token = centroids[code] + bucket_weights[per-dimension index]
+// (optionally L2-normalised), decoded on chip by the dense kernel's decoder warps.
+// ------------------------------------------------------------------------------------------------
+extern "C" size_t tms_residual_workspace_size(int64_t n_queries, int64_t nq, int64_t d,
+                                              int64_t n_docs) {
+  if (n_queries <= 0 || nq <= 0 || d <= 0 || d > 128 || d % 64 != 0 || n_docs < 0) return 0;
+  return tms_dense_workspace_size(TMS_F16, n_queries, nq, d, n_docs, TMS_OUT_SCORE);
+}
+
+extern "C" int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,
+                                   const void* centroids, int64_t n_centroids, const int32_t* codes,
+                                   const uint8_t* residuals, const float* bucket_weights, int nbits,
+                                   int normalize, int64_t n_tokens, const int64_t* doc_offsets,
+                                   int64_t n_docs, int64_t nd_uniform, float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  tms::NvtxRange nvtx_range("tms_residual_maxsim");
+  if (n_queries < 0 || nq <= 0 || d <= 0 || n_docs < 0 || n_tokens < 0 || n_centroids < 1)
+    return TMS_ERR_INVALID;
+  if (nbits != 1 && nbits != 2 && nbits != 4) return TMS_ERR_INVALID;
+  if (d % 64 != 0 || d > 128) return TMS_ERR_UNSUPPORTED;
+  if (n_queries == 0 || n_docs == 0) return TMS_OK;
+  if (!Q || !centroids || !bucket_weights || !out || (n_tokens > 0 && (!codes || !residuals)))
+    return TMS_ERR_INVALID;
+  if (!doc_offsets && (nd_uniform < 0 || n_docs * nd_uniform > n_tokens)) return TMS_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(centroids) & 15) || (reinterpret_cast<uintptr_t>(residuals) & 3) ||
+      (reinterpret_cast<uintptr_t>(codes) & 3))
+    return TMS_ERR_INVALID;  // 16-byte centroid rows, 32-bit residual words and codes
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) {  // every document is empty
+    int status = TMS_OK;
+    const tms::DeviceInfo* dev = tms::current_device_info(&status);
+    if (!dev) return status;
+    const int64_t total = n_queries * n_docs;
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+    tms::fill_kernel<<<blocks, 256, 0, st>>>(out, total, tms::kNegInf);
+    return tms::cuda_status(cudaGetLastError());
+  }
+  return tms::decoder_maxsim<true>(
+      Q, n_queries, nq, d, /* fp32 bucket weights, up to 16 */ 64u, n_tokens, doc_offsets, n_docs,
+      nd_uniform, out, workspace, workspace_bytes, st, [&](tms::DenseArgs& a) {
+        a.res_centroids = static_cast<const __half*>(centroids);
+        a.res_codes = codes;
+        a.res_bits = residuals;
+        a.res_bw = bucket_weights;
+        a.res_ncent = n_centroids;
+        a.res_nbits = nbits;
+        a.res_normalize = normalize ? 1 : 0;
+      });
 }
