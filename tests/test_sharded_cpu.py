@@ -78,6 +78,13 @@ def test_merge_short_shard_padded():
     run([30, 500], k=50)  # rank 0 has fewer documents than k: padded with (NaN, max id)
 
 
+def _exit_flushed(q):
+    """os._exit skips the queue's feeder thread: flush what was put before leaving."""
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
 def _faulty_worker(rank, world, port, mode, q):
     import datetime
     import time
@@ -88,7 +95,7 @@ def _faulty_worker(rank, world, port, mode, q):
     except Exception as e:
         if rank == 0:
             q.put(("setup failed: " + type(e).__name__, -1.0))
-        os._exit(0)
+        _exit_flushed(q)
     if rank == 1:  # leaves between steps, with no collective in flight
         if mode == "stalls":
             time.sleep(10)
@@ -102,7 +109,7 @@ def _faulty_worker(rank, world, port, mode, q):
         q.put(("completed", time.monotonic() - t0))
     except Exception as e:  # the failure reaches the host as an exception, not a hang
         q.put((type(e).__name__, time.monotonic() - t0))
-    os._exit(0)  # no process-group teardown: it would wait for the missing rank
+    _exit_flushed(q)  # no process-group teardown: it would wait for the missing rank
 
 
 @pytest.mark.parametrize("mode", ["dies", "stalls"])
