@@ -27,7 +27,7 @@ def _corpus(d, nbits, seed, n_docs=400, hi=150, n_cent=1000):
 
 @pytest.mark.parametrize("nqry,nq,nbits,normalize,d", [
     (1, 32, 2, True, 128), (5, 32, 2, True, 128), (3, 32, 1, False, 128), (2, 32, 4, True, 128),
-    (1, 40, 2, True, 128), (1, 32, 2, True, 64), (6, 20, 4, False, 64)])
+    (1, 40, 2, True, 128), (1, 32, 2, True, 64), (6, 20, 4, False, 64), (2, 32, 1, True, 64)])
 def test_residual_vs_oracle(nqry, nq, nbits, normalize, d, cuda_device):
     from tilemaxsim_b200 import ResidualMaxSim
     cent, codes, res, bw, off = _corpus(d, nbits, seed=nqry + 10 * nbits + d)
@@ -60,3 +60,27 @@ def test_residual_empty_corpus_and_code_clamp(cuda_device):
     want = O.maxsim_ragged(Q.cpu(), torch.from_numpy(O.residual_decompress(cent, wild, res, bw, 2)), off)
     inf = np.isinf(want)
     np.testing.assert_allclose(got.cpu().numpy()[~inf], want[~inf], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("d,nbits,misalign", [(64, 1, 0), (128, 2, 4), (128, 4, 0)])
+def test_residual_long_ranges_and_copy_widths(d, nbits, misalign, cuda_device):
+    """Dozens of 128-token tiles per CTA (the shared-memory ring wraps many times), residual rows
+    copied 4 bytes at a time (8-byte rows, or a residual buffer that is only 4-byte aligned) or 16
+    at a time."""
+    from tilemaxsim_b200 import ResidualMaxSim
+    cent, codes, res, bw, off = _corpus(d, nbits, seed=21 + d + nbits, n_docs=8000, n_cent=4096)
+    rb = res.shape[1]
+    res_d = res.to(cuda_device)
+    if misalign:
+        buf = torch.zeros(res.numel() + 16, dtype=torch.uint8, device=cuda_device)
+        res_d = buf[misalign:misalign + res.numel()].view(-1, rb)
+        res_d.copy_(res.to(cuda_device))
+        assert res_d.data_ptr() % 16 == misalign
+    Q = R.normalized((2, 32, d), 9)
+    scorer = ResidualMaxSim(cent.to(cuda_device), bw.to(cuda_device), nbits)
+    got = scorer.score_queries(Q.to(cuda_device), codes.to(cuda_device), res_d,
+                               torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.maxsim_ragged(Q, torch.from_numpy(O.residual_decompress(cent, codes, res, bw, nbits)), off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)

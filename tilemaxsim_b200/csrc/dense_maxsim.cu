@@ -51,6 +51,9 @@ constexpr int kThreads = 320;    // 2 control warps + 8 epilogue warps
 constexpr int kPqThreadsMma = 448;  // + 4 decoder warps (PQ variant)
 constexpr int kDecodeWarp0 = 10;
 constexpr int kEpiWarps = 8;
+// Named barriers (0 is __syncthreads): each id belongs to one fixed group of warps.
+constexpr int kBarEpilogue = 1;    // the 8 epilogue warps (column-split mode)
+constexpr int kBarResDecode = 2;   // the 4 residual decoder warps
 constexpr int kQTileRows = 128;
 constexpr uint32_t kQChunkBytes = kQTileRows * 128;  // one 128-row x 128-byte K chunk of Q
 constexpr float kNegInf = -__builtin_huge_valf();
@@ -165,115 +168,227 @@ __device__ __forceinline__ float range_max32(float acc, const uint32_t (&r)[32],
   return fmaxf(m0, m1);
 }
 
-// One residual-compressed token row (d <= 128 values) rebuilt into a swizzled stage row:
-// value j = centroid[j] + bwr[nbits-wide field of residual byte j / (8 / NB)], optionally scaled
-// to unit length (a first pass over the values gives the norm), rounded once to fp16. Each
-// 16-byte unit (8 dimensions) pairs with its NB residual bytes, read as one little-endian
-// integer, so every shift is a compile-time constant.
-template <int NB>
-__device__ __forceinline__ uint32_t residual_unit_bits(const uint8_t* rrow, int u) {
-  if (NB == 4) return __ldg(reinterpret_cast<const uint32_t*>(rrow) + u);
-  if (NB == 2) return __ldg(reinterpret_cast<const unsigned short*>(rrow) + u);
-  return __ldg(rrow + u);
-}
-template <int NB>
-__device__ __forceinline__ float residual_value(const uint4& c, uint32_t bits, const float* bwr, int e) {
-  constexpr int kPerByte = 8 / NB;
-  constexpr uint32_t kMask = (1u << NB) - 1u;
-  const uint32_t cw = (e < 2) ? c.x : (e < 4) ? c.y : (e < 6) ? c.z : c.w;
-  const float cv = __half2float(__ushort_as_half(static_cast<unsigned short>((e & 1) ? (cw >> 16) : (cw & 0xffffu))));
-  const int lb = e / kPerByte, q = e % kPerByte;  // byte within the unit's bits, field within it
-  return cv + bwr[(bits >> (8 * lb + 8 - NB * (q + 1))) & kMask];
-}
-// A quarter of one token (dimensions [d/4 * h, d/4 * (h + 1)): `upp` = d / 32 units of 8), held
-// by one of the four decoder threads that share the token.
-struct ResPart {
-  uint4 c[4];       // centroid units
-  uint32_t b[4];    // each unit's residual bits
+// Residual decoding works from a two-slot ring of shared memory that the decoder warps fill one
+// tile ahead with asynchronous copies, so the L2 gathers of centroid rows overlap the decoding of
+// the previous tile instead of stalling it. Before the ring, a byte table: for each byte value,
+// the bucket weights of the 8 / nbits dimensions that byte encodes (the first dimension in the
+// byte's high bits).
+constexpr int kResRing = 2;
+struct ResLayout {
+  uint32_t table_off, slot_off, slot_bytes, bits_off, pitch, rb, total;
 };
+__host__ __device__ inline ResLayout residual_layout(int d, int nb) {
+  ResLayout R;
+  R.pitch = static_cast<uint32_t>(2 * d);
+  R.rb = static_cast<uint32_t>(d * nb / 8);
+  R.table_off = 8u * kResRing;                                   // after the ring's mbarriers
+  R.slot_off = (R.table_off + 256u * (8u / nb) * 4u + 127u) & ~127u;
+  R.bits_off = 128u * R.pitch;                                  // 128-token tiles
+  R.slot_bytes = (R.bits_off + 128u * R.rb + 127u) & ~127u;
+  R.total = R.slot_off + kResRing * R.slot_bytes;
+  return R;
+}
+
+// Adds the bucket weights of one 8-dimension unit (its NB residual bytes, little-endian in
+// `bits`) to the unit's centroid values.
 template <int NB>
-__device__ __forceinline__ void res_part_load(ResPart& P, const uint4* crow, const uint8_t* rrow,
-                                              int u0, int upp, bool valid) {
+__device__ __forceinline__ void residual_unit(const uint4& c, uint32_t bits, const float* table,
+                                              float (&x)[8]) {
+  const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool on = valid && i < upp;
-    P.c[i] = on ? __ldg(crow + u0 + i) : make_uint4(0, 0, 0, 0);
-    P.b[i] = on ? residual_unit_bits<NB>(rrow, u0 + i) : 0u;
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
+    x[2 * k] = f.x;
+    x[2 * k + 1] = f.y;
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const uint32_t v = (bits >> (8 * b)) & 0xffu;
+    if (NB == 1) {
+      const float4 w0 = reinterpret_cast<const float4*>(table)[2 * v];
+      const float4 w1 = reinterpret_cast<const float4*>(table)[2 * v + 1];
+      x[0] += w0.x; x[1] += w0.y; x[2] += w0.z; x[3] += w0.w;
+      x[4] += w1.x; x[5] += w1.y; x[6] += w1.z; x[7] += w1.w;
+    } else if (NB == 2) {
+      const float4 w = reinterpret_cast<const float4*>(table)[v];
+      x[4 * b] += w.x; x[4 * b + 1] += w.y; x[4 * b + 2] += w.z; x[4 * b + 3] += w.w;
+    } else {
+      const float2 w = reinterpret_cast<const float2*>(table)[v];
+      x[2 * b] += w.x; x[2 * b + 1] += w.y;
+    }
   }
 }
-// Values of the part, scaled by the token's norm (a sum over the four threads of the token, lanes
-// 4k..4k+3), rounded to fp16 and stored in the swizzled stage row. Every lane of the warp calls it.
-template <int NB, int TN>
-__device__ __forceinline__ void res_part_store(const ResPart& P, const float* bwr, int u0, int upp,
-                                               bool normalize, bool valid, uint8_t* rowp, uint32_t sw) {
-  float scale = 1.0f;
-  if (normalize) {
-    float ss = 0.0f;
+
+// The residual decoder role (4 warps, thread dt = 0..127) for NB bits per dimension and D = 64 or
+// 128 dimensions, compiled per (NB, D) so every loop below has a fixed trip count.
+//
+// Ring: tile i + 1's centroid rows and residual bytes are copied (cp.async) into ring slot
+// (i + 1) % 2 while tile i is decoded from slot i % 2. Each warp gathers the centroid rows of its
+// own 32 tokens in 16-byte pieces (consecutive lanes on consecutive pieces of a row; a row's
+// centroid id comes from its token's lane by shuffle); the tile's residual bytes are contiguous
+// and copied in 16-byte (or, for 8-byte rows or a residual buffer that is only 4-byte aligned,
+// 4-byte) pieces. Every thread's copies arrive on the slot's mbarrier (128 arrivals).
+//
+// Decoding: in pass p, thread dt takes token 16 p + dt / 8 and its 16-byte units h and h + 8
+// (h = dt % 8), so the eight lanes of a token read 128 contiguous bytes of the row (every bank once
+// per phase) and add up the squared values for the norm with three shuffles. Values are
+// centroid + bucket weight in fp32, scaled by the token's inverse norm, rounded once to fp16 and
+// stored in the 128-byte-swizzle layout (unit u of row r at u ^ (r % 8)).
+//
+// A named barrier over the 128 decoder threads closes each tile (the slot it read is free again)
+// and ORs the failure flag, so the four warps always leave the loop together; copies still in
+// flight after a failure land before the CTA exits.
+template <int NB, int D>
+__device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* smem, const SmemLayout& L,
+                                                  uint32_t bar_s, int S, int64_t tok_lo, int64_t tok_hi,
+                                                  volatile int* abort_flag, uint64_t tmo) {
+  constexpr int UPP = D / 64;   // 16-byte units per thread per token
+  constexpr int CPR = D / 8;    // 16-byte pieces per centroid row
+  constexpr int RPS = 32 / CPR; // rows per warp-wide gather step
+  constexpr int RB = D * NB / 8;  // residual bytes per token
+  constexpr int PITCH = 2 * D;
+  const int dt = static_cast<int>(threadIdx.x) - kDecodeWarp0 * 32;
+  const int lane = dt & 31, tw = dt & ~31;
+  const ResLayout R = residual_layout(D, NB);
+  uint8_t* cbase = smem + L.cb_off;
+  const uint32_t ring_bar = smem_u32(cbase);
+  const float* table = reinterpret_cast<const float*>(cbase + R.table_off);
+  const bool w16 = (RB % 16 == 0) && (reinterpret_cast<uintptr_t>(a.res_bits) & 15) == 0;
+  const int64_t ncent = a.res_ncent;
+  const bool nrm = a.res_normalize != 0;
+  const int64_t n_tiles = (tok_hi - tok_lo + 127) / 128;
+  auto full_bar = [&](int s) { return bar_s + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_s + 8u * (S + s); };
+
+  int32_t code_next = tok_lo + dt < tok_hi ? __ldg(a.res_codes + tok_lo + dt) : 0;
+  auto issue = [&](int64_t j) {
+    const int64_t t0 = tok_lo + 128 * j;
+    const int sl = static_cast<int>(j % kResRing);
+    const uint32_t slot = smem_u32(cbase + R.slot_off + sl * R.slot_bytes);
+    int32_t c = code_next;
+    code_next = t0 + 128 + dt < tok_hi ? __ldg(a.res_codes + t0 + 128 + dt) : 0;
+    c = c < 0 ? 0 : (c >= ncent ? static_cast<int32_t>(ncent - 1) : c);  // never outside the table
+    const int n = static_cast<int>(min(int64_t(128), tok_hi - t0));
+    const int pc = lane % CPR;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (i >= upp) break;
+    for (int m = 0; m < CPR; ++m) {
+      const int tl = m * RPS + lane / CPR;  // token within the warp's 32
+      const int32_t cc = __shfl_sync(0xffffffffu, c, tl);
+      if (tw + tl < n)
+        cp_async16(slot + static_cast<uint32_t>((tw + tl) * PITCH + 16 * pc),
+                   a.res_centroids + static_cast<int64_t>(cc) * D + 8 * pc);
+    }
+    const uint8_t* src = a.res_bits + t0 * RB;
+    const uint32_t dst = slot + R.bits_off;
+    if (RB % 16 == 0 && w16) {
+      const int lim = n * (RB / 16);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float x = residual_value<NB>(P.c[i], P.b[i], bwr, e);
-        ss = fmaf(x, x, ss);
+      for (int q = 0; q < (8 * RB + 127) / 128; ++q) {
+        const int k = dt + 128 * q;
+        if (k < lim) cp_async16(dst + 16u * k, src + 16 * k);
+      }
+    } else {
+      const int lim = n * (RB / 4);
+#pragma unroll
+      for (int q = 0; q < (32 * RB + 127) / 128; ++q) {
+        const int k = dt + 128 * q;
+        if (k < lim) cp_async4(dst + 4u * k, src + 4 * k);
       }
     }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    scale = ss > 0.0f ? rsqrtf(ss) : 0.0f;
-  }
-  if (!valid) return;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (i >= upp) break;
-    const int u = u0 + i;
-    uint32_t pk[4];
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const __half2 h = __floats2half2_rn(residual_value<NB>(P.c[i], P.b[i], bwr, e) * scale,
-                                          residual_value<NB>(P.c[i], P.b[i], bwr, e + 1) * scale);
-      pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    *reinterpret_cast<uint4*>(rowp + (u >> 3) * (TN * 128) + (((static_cast<uint32_t>(u) & 7u) ^ sw) << 4)) =
-        make_uint4(pk[0], pk[1], pk[2], pk[3]);
-  }
-}
-// One tile (TN = 128 tokens) decoded by 128 threads: thread dt holds part dt % 4 of token
-// 32 p + dt / 4 in pass p (4 passes); the next pass's loads are issued before this pass's math.
-template <int NB, int TN>
-__device__ __forceinline__ void decode_residual_tile(const int32_t (&code)[4], int64_t t0, int64_t tok_hi,
-                                                     int dt, int d, const __half* cent, int64_t ncent,
-                                                     const uint8_t* res_bits, const float* bwr,
-                                                     bool normalize, uint8_t* stage) {
-  const int tk = dt >> 2, h = dt & 3;
-  const int upp = d / 32, u0 = h * upp;
-  const int64_t rbytes = static_cast<int64_t>(d) * NB / 8;
-  auto src = [&](int p, const uint4*& crow, const uint8_t*& rrow) -> bool {
-    const int64_t tok = t0 + 32 * p + tk;
-    const bool v = tok < tok_hi;
-    int32_t c = code[p];
-    c = c < 0 ? 0 : (c >= ncent ? static_cast<int32_t>(ncent - 1) : c);  // never outside the table
-    crow = reinterpret_cast<const uint4*>(cent + static_cast<int64_t>(c) * d);
-    rrow = res_bits + (v ? tok : 0) * rbytes;
-    return v;
+    cp_async_mbar_arrive_noinc(ring_bar + 8u * sl);
   };
-  ResPart cur, nxt;
-  const uint4* crow;
-  const uint8_t* rrow;
-  bool v_cur = src(0, crow, rrow);
-  res_part_load<NB>(cur, crow, rrow, u0, upp, v_cur);
+
+  auto decode = [&](const uint8_t* slot, int n_valid, uint8_t* stage) {
+    const int tk = dt >> 3, h = dt & 7;
+#pragma unroll 2
+    for (int p = 0; p < 8; ++p) {
+      const int r = 16 * p + tk;
+      const uint8_t* crow = slot + r * PITCH;
+      const uint8_t* brow = slot + R.bits_off + r * RB;
+      float x[UPP][8];
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    bool v_nxt = false;
-    if (p + 1 < 4) {
-      v_nxt = src(p + 1, crow, rrow);
-      res_part_load<NB>(nxt, crow, rrow, u0, upp, v_nxt);
+      for (int i = 0; i < UPP; ++i) {
+        const int u = h + 8 * i;
+        const uint4 c = *reinterpret_cast<const uint4*>(crow + u * 16);
+        uint32_t bits;
+        if (NB == 4) bits = *reinterpret_cast<const uint32_t*>(brow + u * 4);
+        else if (NB == 2) bits = *reinterpret_cast<const unsigned short*>(brow + u * 2);
+        else bits = brow[u];
+        residual_unit<NB>(c, bits, table, x[i]);
+      }
+      float scale = 1.0f;
+      if (nrm) {
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < UPP; ++i)
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            s0 = fmaf(x[i][e], x[i][e], s0);
+            s1 = fmaf(x[i][e + 1], x[i][e + 1], s1);
+          }
+        float ss = s0 + s1;
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+        scale = ss > 0.0f ? rsqrtf(ss) : 0.0f;
+      }
+      if (r < n_valid) {
+        uint8_t* rowp = stage + r * 128;
+        const uint32_t sw = static_cast<uint32_t>(r & 7);
+#pragma unroll
+        for (int i = 0; i < UPP; ++i) {
+          const int u = h + 8 * i;
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const __half2 hv = __floats2half2_rn(x[i][e] * scale, x[i][e + 1] * scale);
+            pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(rowp + (u >> 3) * (128 * 128) + (((static_cast<uint32_t>(u) & 7u) ^ sw) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
     }
-    const int r = 32 * p + tk;
-    res_part_store<NB, TN>(cur, bwr, u0, upp, normalize, v_cur, stage + r * 128, static_cast<uint32_t>(r & 7));
-    if (p + 1 < 4) {
-      cur = nxt;
-      v_cur = v_nxt;
+  };
+
+  int s = 0;
+  uint32_t ph = 0;
+  bool ok = !(a.debug_flags & 1);
+  int64_t issued = 0;
+  if (ok && n_tiles > 0) {
+    issue(0);
+    issued = 1;
+  }
+  for (int64_t i = 0; ok && i < n_tiles; ++i) {
+    if (i + 1 < n_tiles) {
+      issue(i + 1);
+      issued = i + 2;
+    }
+    int w = 0;
+    if (lane == 0) w = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 10);
+    bool good = __shfl_sync(0xffffffffu, w, 0) != 0;
+    const int sl = static_cast<int>(i % kResRing);
+    if (good)
+      good = mbar_wait(ring_bar + 8u * sl, static_cast<uint32_t>((i / kResRing) & 1), abort_flag, tmo,
+                       a.err, 11);
+    good = __all_sync(0xffffffffu, good);
+    if (good) {
+      const int64_t t0 = tok_lo + 128 * i;
+      decode(cbase + R.slot_off + sl * R.slot_bytes, static_cast<int>(min(int64_t(128), tok_hi - t0)),
+             smem + L.stage_off + static_cast<size_t>(s) * L.stage_bytes);
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full_bar(s));
+    }
+    if (++s == S) { s = 0; ph ^= 1u; }
+    ok = !named_barrier_or(kBarResDecode, 128, !good);
+  }
+  cp_async_wait_all();
+  for (int64_t j = issued >= 2 ? issued - 2 : 0; !ok && j < issued; ++j) {
+    const uint32_t bar = ring_bar + 8u * static_cast<uint32_t>(j % kResRing);
+    const uint32_t par = static_cast<uint32_t>((j / kResRing) & 1);
+    const uint64_t tw0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, par) && globaltimer_ns() - tw0 < tmo) {
     }
   }
 }
@@ -327,6 +442,8 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     }
     mbar_init(qfull_bar, 1);
     mbar_init(done_bar, 1);
+    if (RES)  // residual ring slots: one cp.async arrival per decoder thread
+      for (int b = 0; b < kResRing; ++b) mbar_init(smem_u32(smem + L.cb_off) + 8u * b, 128);
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
     if (*abort_flag) atomicCAS(a.err, 0u, kDevErrTimeout | 15u);
     fence_mbar_init();
@@ -356,14 +473,18 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
   }
   if (PQ) {  // stage the codebook in shared memory as fp16 (every thread helps)
     __half* cbs = reinterpret_cast<__half*>(smem + L.cb_off);
-    if (a.res_nbits) {
-      // entry v = the weight of the bucket whose index is v's nbits bits reversed: the packing
-      // puts a dimension's lowest index bit first (highest in its byte field), so a field read
-      // as a plain number indexes this table directly
-      float* bws = reinterpret_cast<float*>(smem + L.cb_off);
-      const int nb = a.res_nbits;
-      for (int v = threadIdx.x; v < (1 << nb); v += blockDim.x)
-        bws[v] = a.res_bw[__brev(static_cast<unsigned>(v)) >> (32 - nb)];
+    if (RES) {
+      // byte table: entry v, field q = the weight of the bucket whose index has bit k equal to
+      // bit (7 - q * nbits - k) of v (the packing is MSB-first, lowest index bit first)
+      const int nb = a.res_nbits, per = 8 / nb;
+      const ResLayout R = residual_layout(a.kc * 64, nb);
+      float* table = reinterpret_cast<float*>(smem + L.cb_off + R.table_off);
+      for (int i = threadIdx.x; i < 256 * per; i += blockDim.x) {
+        const int v = i / per, q = i - v * per;
+        int idx = 0;
+        for (int k = 0; k < nb; ++k) idx |= ((v >> (7 - q * nb - k)) & 1) << k;
+        table[i] = a.res_bw[idx];
+      }
     }
     const int n = a.res_nbits ? 0 : a.pq_M * a.pq_K * a.pq_dsub;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -432,49 +553,15 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     }
   } else if (PQ && RES && warp >= kDecodeWarp0) {
     // ------------------------------------------------------------------ residual decoders
-    // Row r of a D stage = token t0 + r: centroids[code] + bucket_weights[index of each dimension]
-    // (optionally scaled to unit length), rounded once to fp16, written in the 128-byte-swizzle
-    // layout (unit u of row r at u ^ (r % 8)). Four threads share a token (a quarter of its d <= 128
-    // dimensions each). A dimension's index is the nbits-wide field of its residual byte
-    // (MSB-first packing), looked up in the bit-reversed weight table staged above.
-    const float* bwr = reinterpret_cast<const float*>(smem + L.cb_off);
-    const int dt = threadIdx.x - kDecodeWarp0 * 32;  // 0..127
-    const int d = a.kc * 64;
     const int nb = a.res_nbits;
-    const int64_t ncent = a.res_ncent;
-    const bool nrm = a.res_normalize != 0;
-    int s = 0;
-    uint32_t ph = 0;
-    bool ok = !(a.debug_flags & 1);
-    // the centroid ids of the next tile's four passes are loaded while this tile is decoded
-    int32_t code_n[4];
-    auto load_codes = [&](int64_t t0) {
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int64_t tok = t0 + 32 * p + (dt >> 2);
-        code_n[p] = tok < tok_hi ? __ldg(a.res_codes + tok) : 0;
-      }
-    };
-    load_codes(tok_lo);
-    for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
-      int32_t code[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) code[p] = code_n[p];
-      load_codes(t0 + TN);
-      int w = 0;
-      if (lane == 0) w = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 10);
-      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
-      uint8_t* stage = smem + L.stage_off + static_cast<size_t>(s) * L.stage_bytes;
-      if (nb == 2)
-        decode_residual_tile<2, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
-      else if (nb == 1)
-        decode_residual_tile<1, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
-      else
-        decode_residual_tile<4, TN>(code, t0, tok_hi, dt, d, a.res_centroids, ncent, a.res_bits, bwr, nrm, stage);
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
-      __syncwarp();
-      if (lane == 0) mbar_arrive(full_bar(s));
-      if (++s == S) { s = 0; ph ^= 1u; }
+    if (a.kc == 2) {
+      if (nb == 2) residual_decoders<2, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else if (nb == 1) residual_decoders<1, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else residual_decoders<4, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+    } else {
+      if (nb == 2) residual_decoders<2, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else if (nb == 1) residual_decoders<1, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else residual_decoders<4, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
     }
   } else if (PQ && !RES && warp >= kDecodeWarp0) {
     // ------------------------------------------------------------------ PQ decoders
@@ -735,10 +822,10 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
         asm volatile(
             "{\n\t.reg .pred p, q;\n\t"
             "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.and.pred q, 1, %2, p;\n\t"
+            "bar.red.and.pred q, %3, %2, p;\n\t"
             "selp.u32 %0, 1, 0, q;\n\t}\n"
             : "=r"(all_ok)
-            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32)
+            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32), "n"(kBarEpilogue)
             : "memory");
         if (!(ok = all_ok != 0)) break;
         const int n_parts = (ncol + 31) / 32;
@@ -890,10 +977,10 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
         asm volatile(
             "{\n\t.reg .pred p, q;\n\t"
             "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.and.pred q, 1, %2, p;\n\t"
+            "bar.red.and.pred q, %3, %2, p;\n\t"
             "selp.u32 %0, 1, 0, q;\n\t}\n"
             : "=r"(all_ok)
-            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32)
+            : "r"(static_cast<uint32_t>(w_ok)), "n"(kEpiWarps * 32), "n"(kBarEpilogue)
             : "memory");
         if (!(ok = all_ok != 0)) break;
         const int n_parts = (ncol + PC - 1) / PC;
@@ -1386,6 +1473,7 @@ int decoder_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d, uint
                       dev->max_smem_optin, &p, cb_bytes,
                       /* 128-token tiles: two query tiles per CTA fit beside the codebook */ 128);
   if (rc != TMS_OK) return rc;
+  if (RES && p.TN != 128) return TMS_ERR_UNSUPPORTED;  // the residual decoders fill 128-token tiles
   if (!workspace || workspace_bytes < p.qp_bytes + p.partial_bytes) return TMS_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 1023) return TMS_ERR_INVALID;
   uint8_t* qp = static_cast<uint8_t*>(workspace);
@@ -1426,10 +1514,12 @@ int decoder_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d, uint
   args.cb_bytes = cb_bytes;
   args.debug_flags = debug_flags();
   fill(args);
-  if (p.TN == 256)
-    rc = launch_dense_t<256, true, false, true, RES>(qm, qm, args, p, st);
+  if constexpr (RES)
+    rc = launch_dense_t<128, true, false, true, true>(qm, qm, args, p, st);
+  else if (p.TN == 256)
+    rc = launch_dense_t<256, true, false, true, false>(qm, qm, args, p, st);
   else
-    rc = launch_dense_t<128, true, false, true, RES>(qm, qm, args, p, st);
+    rc = launch_dense_t<128, true, false, true, false>(qm, qm, args, p, st);
   if (rc != TMS_OK || p.nchunk == 1) return rc;
   const int64_t total = n_queries * n_docs;
   blocks = static_cast<int>((total + 255) / 256);
@@ -1554,7 +1644,7 @@ extern "C" int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq,
     return tms::cuda_status(cudaGetLastError());
   }
   return tms::decoder_maxsim<true>(
-      Q, n_queries, nq, d, /* fp32 bucket weights, up to 16 */ 64u, n_tokens, doc_offsets, n_docs,
+      Q, n_queries, nq, d, tms::residual_layout(static_cast<int>(d), nbits).total, n_tokens, doc_offsets, n_docs,
       nd_uniform, out, workspace, workspace_bytes, st, [&](tms::DenseArgs& a) {
         a.res_centroids = static_cast<const __half*>(centroids);
         a.res_codes = codes;
