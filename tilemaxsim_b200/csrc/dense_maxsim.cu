@@ -49,11 +49,14 @@ namespace {
 
 constexpr int kThreads = 320;    // 2 control warps + 8 epilogue warps
 constexpr int kPqThreadsMma = 448;  // + 4 decoder warps (PQ variant)
+// residual variant: RES decoder warps after the 10 warps of the dense kernel
+constexpr int kResDecWarps = 8;
+constexpr int res_threads(int res_warps) { return (10 + res_warps) * 32; }
 constexpr int kDecodeWarp0 = 10;
 constexpr int kEpiWarps = 8;
 // Named barriers (0 is __syncthreads): each id belongs to one fixed group of warps.
 constexpr int kBarEpilogue = 1;    // the 8 epilogue warps (column-split mode)
-constexpr int kBarResDecode = 2;   // the 4 residual decoder warps
+constexpr int kBarResDecode = 2;   // the residual decoder warps
 constexpr int kQTileRows = 128;
 constexpr uint32_t kQChunkBytes = kQTileRows * 128;  // one 128-row x 128-byte K chunk of Q
 constexpr float kNegInf = -__builtin_huge_valf();
@@ -219,26 +222,26 @@ __device__ __forceinline__ void residual_unit(const uint4& c, uint32_t bits, con
   }
 }
 
-// The residual decoder role (4 warps, thread dt = 0..127) for NB bits per dimension and D = 64 or
+// The residual decoder role (DW warps, thread dt = 0 .. 32 DW - 1) for NB bits per dimension and D = 64 or
 // 128 dimensions, compiled per (NB, D) so every loop below has a fixed trip count.
 //
 // Ring: tile i + 1's centroid rows and residual bytes are copied (cp.async) into ring slot
 // (i + 1) % 2 while tile i is decoded from slot i % 2. Each warp gathers the centroid rows of its
-// own 32 tokens in 16-byte pieces (consecutive lanes on consecutive pieces of a row; a row's
+// own 16 tokens in 16-byte pieces (consecutive lanes on consecutive pieces of a row; a row's
 // centroid id comes from its token's lane by shuffle); the tile's residual bytes are contiguous
 // and copied in 16-byte (or, for 8-byte rows or a residual buffer that is only 4-byte aligned,
-// 4-byte) pieces. Every thread's copies arrive on the slot's mbarrier (128 arrivals).
+// 4-byte) pieces. Every thread's copies arrive on the slot's mbarrier (256 arrivals).
 //
-// Decoding: in pass p, thread dt takes token 16 p + dt / 8 and its 16-byte units h and h + 8
+// Decoding: in pass p (of 4), thread dt takes token 32 p + dt / 8 and its 16-byte units h and h + 8
 // (h = dt % 8), so the eight lanes of a token read 128 contiguous bytes of the row (every bank once
 // per phase) and add up the squared values for the norm with three shuffles. Values are
 // centroid + bucket weight in fp32, scaled by the token's inverse norm, rounded once to fp16 and
 // stored in the 128-byte-swizzle layout (unit u of row r at u ^ (r % 8)).
 //
-// A named barrier over the 128 decoder threads closes each tile (the slot it read is free again)
+// A named barrier over the 256 decoder threads closes each tile (the slot it read is free again)
 // and ORs the failure flag, so the four warps always leave the loop together; copies still in
 // flight after a failure land before the CTA exits.
-template <int NB, int D>
+template <int NB, int D, int DW>
 __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* smem, const SmemLayout& L,
                                                   uint32_t bar_s, int S, int64_t tok_lo, int64_t tok_hi,
                                                   volatile int* abort_flag, uint64_t tmo) {
@@ -247,8 +250,11 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
   constexpr int RPS = 32 / CPR; // rows per warp-wide gather step
   constexpr int RB = D * NB / 8;  // residual bytes per token
   constexpr int PITCH = 2 * D;
+  constexpr int NT = DW * 32;   // decoder threads
+  constexpr int TPW = 128 / DW;  // tokens of a tile each warp gathers
   const int dt = static_cast<int>(threadIdx.x) - kDecodeWarp0 * 32;
-  const int lane = dt & 31, tw = dt & ~31;
+  const int lane = dt & 31, tw = (dt >> 5) * TPW;
+  const int tc = tw + (lane % TPW);  // the token whose centroid id this thread holds
   const ResLayout R = residual_layout(D, NB);
   uint8_t* cbase = smem + L.cb_off;
   const uint32_t ring_bar = smem_u32(cbase);
@@ -260,19 +266,19 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
   auto full_bar = [&](int s) { return bar_s + 8u * s; };
   auto empty_bar = [&](int s) { return bar_s + 8u * (S + s); };
 
-  int32_t code_next = tok_lo + dt < tok_hi ? __ldg(a.res_codes + tok_lo + dt) : 0;
+  int32_t code_next = tok_lo + tc < tok_hi ? __ldg(a.res_codes + tok_lo + tc) : 0;
   auto issue = [&](int64_t j) {
     const int64_t t0 = tok_lo + 128 * j;
     const int sl = static_cast<int>(j % kResRing);
     const uint32_t slot = smem_u32(cbase + R.slot_off + sl * R.slot_bytes);
     int32_t c = code_next;
-    code_next = t0 + 128 + dt < tok_hi ? __ldg(a.res_codes + t0 + 128 + dt) : 0;
+    code_next = t0 + 128 + tc < tok_hi ? __ldg(a.res_codes + t0 + 128 + tc) : 0;
     c = c < 0 ? 0 : (c >= ncent ? static_cast<int32_t>(ncent - 1) : c);  // never outside the table
     const int n = static_cast<int>(min(int64_t(128), tok_hi - t0));
     const int pc = lane % CPR;
 #pragma unroll
-    for (int m = 0; m < CPR; ++m) {
-      const int tl = m * RPS + lane / CPR;  // token within the warp's 32
+    for (int m = 0; m < TPW / RPS; ++m) {
+      const int tl = m * RPS + lane / CPR;  // token within the warp's TPW
       const int32_t cc = __shfl_sync(0xffffffffu, c, tl);
       if (tw + tl < n)
         cp_async16(slot + static_cast<uint32_t>((tw + tl) * PITCH + 16 * pc),
@@ -283,15 +289,15 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
     if (RB % 16 == 0 && w16) {
       const int lim = n * (RB / 16);
 #pragma unroll
-      for (int q = 0; q < (8 * RB + 127) / 128; ++q) {
-        const int k = dt + 128 * q;
+      for (int q = 0; q < (8 * RB + NT - 1) / NT; ++q) {
+        const int k = dt + NT * q;
         if (k < lim) cp_async16(dst + 16u * k, src + 16 * k);
       }
     } else {
       const int lim = n * (RB / 4);
 #pragma unroll
-      for (int q = 0; q < (32 * RB + 127) / 128; ++q) {
-        const int k = dt + 128 * q;
+      for (int q = 0; q < (32 * RB + NT - 1) / NT; ++q) {
+        const int k = dt + NT * q;
         if (k < lim) cp_async4(dst + 4u * k, src + 4 * k);
       }
     }
@@ -301,8 +307,8 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
   auto decode = [&](const uint8_t* slot, int n_valid, uint8_t* stage) {
     const int tk = dt >> 3, h = dt & 7;
 #pragma unroll 2
-    for (int p = 0; p < 8; ++p) {
-      const int r = 16 * p + tk;
+    for (int p = 0; p < 128 * 8 / NT; ++p) {
+      const int r = (NT / 8) * p + tk;
       const uint8_t* crow = slot + r * PITCH;
       const uint8_t* brow = slot + R.bits_off + r * RB;
       float x[UPP][8];
@@ -381,7 +387,7 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
       if (lane == 0) mbar_arrive(full_bar(s));
     }
     if (++s == S) { s = 0; ph ^= 1u; }
-    ok = !named_barrier_or(kBarResDecode, 128, !good);
+    ok = !named_barrier_or(kBarResDecode, NT, !good);
   }
   cp_async_wait_all();
   for (int64_t j = issued >= 2 ? issued - 2 : 0; !ok && j < issued; ++j) {
@@ -393,8 +399,8 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
   }
 }
 
-template <int TN, bool QRES, bool TF32, bool PQ, bool RES = false>
-__global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
+template <int TN, bool QRES, bool TF32, bool PQ, int RES = 0>
+__global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : kThreads, 1)
     dense_maxsim_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap dmap, const DenseArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), PQ ? 4 : 1);  // PQ: one arrival per decoder warp
+      mbar_init(full_bar(s), RES ? RES : PQ ? 4 : 1);  // one arrival per decoder warp
       mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < NSLOT; ++b) {
@@ -443,7 +449,7 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     mbar_init(qfull_bar, 1);
     mbar_init(done_bar, 1);
     if (RES)  // residual ring slots: one cp.async arrival per decoder thread
-      for (int b = 0; b < kResRing; ++b) mbar_init(smem_u32(smem + L.cb_off) + 8u * b, 128);
+      for (int b = 0; b < kResRing; ++b) mbar_init(smem_u32(smem + L.cb_off) + 8u * b, RES * 32);
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
     if (*abort_flag) atomicCAS(a.err, 0u, kDevErrTimeout | 15u);
     fence_mbar_init();
@@ -555,13 +561,13 @@ __global__ void __launch_bounds__(PQ ? kPqThreadsMma : kThreads, 1)
     // ------------------------------------------------------------------ residual decoders
     const int nb = a.res_nbits;
     if (a.kc == 2) {
-      if (nb == 2) residual_decoders<2, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
-      else if (nb == 1) residual_decoders<1, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
-      else residual_decoders<4, 128>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      if (nb == 2) residual_decoders<2, 128, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else if (nb == 1) residual_decoders<1, 128, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else residual_decoders<4, 128, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
     } else {
-      if (nb == 2) residual_decoders<2, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
-      else if (nb == 1) residual_decoders<1, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
-      else residual_decoders<4, 64>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      if (nb == 2) residual_decoders<2, 64, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else if (nb == 1) residual_decoders<1, 64, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
+      else residual_decoders<4, 64, (RES > 0 ? RES : 4)>(a, smem, L, bar_s, S, tok_lo, tok_hi, abort_flag, tmo);
     }
   } else if (PQ && !RES && warp >= kDecodeWarp0) {
     // ------------------------------------------------------------------ PQ decoders
@@ -1275,7 +1281,7 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   return TMS_OK;
 }
 
-template <int TN, bool QRES, bool TF32, bool PQ = false, bool RES = false>
+template <int TN, bool QRES, bool TF32, bool PQ = false, int RES = 0>
 int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs& args,
                    const DensePlan& p, cudaStream_t st) {
   auto kern = dense_maxsim_kernel<TN, QRES, TF32, PQ, RES>;
@@ -1285,7 +1291,7 @@ int launch_dense_t(const CUtensorMap& qm, const CUtensorMap& dm, const DenseArgs
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (e != cudaSuccess) return TMS_ERR_CUDA;
   const unsigned grid = static_cast<unsigned>(p.n_ranges) * static_cast<unsigned>(p.n_groups);
-  kern<<<grid, PQ ? kPqThreadsMma : kThreads, L.total, st>>>(qm, dm, args);
+  kern<<<grid, RES ? res_threads(RES) : PQ ? kPqThreadsMma : kThreads, L.total, st>>>(qm, dm, args);
   return cuda_status(cudaGetLastError());
 }
 
@@ -1514,12 +1520,17 @@ int decoder_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d, uint
   args.cb_bytes = cb_bytes;
   args.debug_flags = debug_flags();
   fill(args);
-  if constexpr (RES)
-    rc = launch_dense_t<128, true, false, true, true>(qm, qm, args, p, st);
-  else if (p.TN == 256)
-    rc = launch_dense_t<256, true, false, true, false>(qm, qm, args, p, st);
-  else
-    rc = launch_dense_t<128, true, false, true, false>(qm, qm, args, p, st);
+  if constexpr (RES) {
+    // eight decoder warps (two per scheduler): the decoding is latency-bound, and the second warp
+    // per scheduler is worth more than the registers it costs (96 per thread at 576 threads, with
+    // a few spills): 18.2 ms against 23.2 ms with four warps at 128 registers (1 query, 1M x 128
+    // tokens, nbits = 2)
+    rc = launch_dense_t<128, true, false, true, kResDecWarps>(qm, qm, args, p, st);
+  } else if (p.TN == 256) {
+    rc = launch_dense_t<256, true, false, true, 0>(qm, qm, args, p, st);
+  } else {
+    rc = launch_dense_t<128, true, false, true, 0>(qm, qm, args, p, st);
+  }
   if (rc != TMS_OK || p.nchunk == 1) return rc;
   const int64_t total = n_queries * n_docs;
   blocks = static_cast<int>((total + 255) / 256);
