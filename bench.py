@@ -229,6 +229,48 @@ def run_reference_pq(args, cfg, rank: int) -> None:
         "gpu_launches": 0})
 
 
+def run_reference_res(args, cfg, rank: int) -> None:
+    """Residual-compressed scoring on the host cores: the oracle's decompress + MaxSim + top-k (the
+    reference names the storage format but has no implementation of this path), on a bounded
+    sample of the workload."""
+    if rank != 0:
+        return
+    from oracle import maxsim_oracle as O
+    nqry, nq, d, nbits, n_cent, n_docs, nd, k = cfg
+    n_s = min(n_docs, 2000)
+    rng = np.random.default_rng(42)
+    cent = torch.nn.functional.normalize(torch.from_numpy(rng.standard_normal((n_cent, d), dtype=np.float32)),
+                                         dim=-1).half()
+    codes = rng.integers(0, n_cent, n_s * nd).astype(np.int32)
+    res = rng.integers(0, 256, (n_s * nd, d * nbits // 8), dtype=np.uint8)
+    off = np.arange(n_s + 1, dtype=np.int64) * nd
+    bw = np.linspace(-0.06, 0.06, 1 << nbits, dtype=np.float32)
+    Q = make_queries(nqry, nq, d, 7)
+
+    def one():
+        D = torch.from_numpy(O.residual_decompress(cent, codes, res, bw, nbits))
+        return O.topk(O.maxsim_ragged(Q, D, off), min(k, n_s))
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    dt = (time.perf_counter() - t0) / args.steps
+    val = nqry * n_s * nd / dt
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    emit_json({
+        "impl": "reference", "metric": "doc-tokens scored/s", "value": val, "unit": "doc-tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config},
+        "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"per step {nqry} queries x {n_s} docs x {nd} residual-compressed tokens, "
+                                   "NumPy decompress + MaxSim restatement"},
+        "e2e": {"value": val, "unit": "doc-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0})
+
+
 def config_dict(args, cfg) -> dict:
     nqry, nq, d, n_docs, lo, hi, k = cfg
     return {"workload": f"{args.config}: {nqry} queries x {nq} tokens vs {n_docs} ragged docs per GPU "
@@ -408,6 +450,110 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "clocks": clocks})
 
 
+RES_CONFIGS = {
+    # name: (n_queries, nq, d, nbits, n_centroids, n_docs per GPU, nd, k): a ColBERTv2-style
+    # residual-compressed corpus (centroid id + 2-bit residuals, 36 bytes per token)
+    "q1_res": (1, 32, 128, 2, 65536, 1_000_000, 128, 100),
+    "q5_res": (5, 32, 128, 2, 65536, 1_000_000, 128, 100),
+}
+
+
+def run_res(args, cfg, rank: int, world: int, device: torch.device) -> None:
+    """Residual-compressed scoring (ResidualMaxSim.score_queries) + per-query top-k."""
+    import tilemaxsim_b200 as tms
+    from tilemaxsim_b200.sharded import merge_topk
+    nqry, nq, d, nbits, n_cent, n_docs, nd, k = cfg
+    T = n_docs * nd
+    g = torch.Generator(device=device).manual_seed(42 + rank)
+    cent = torch.nn.functional.normalize(torch.randn(n_cent, d, generator=g, device=device), dim=-1).half()
+    codes = torch.randint(0, n_cent, (T,), generator=g, device=device, dtype=torch.int32)
+    res = torch.randint(0, 256, (T, d * nbits // 8), generator=g, device=device, dtype=torch.uint8)
+    off = torch.arange(n_docs + 1, device=device, dtype=torch.int64) * nd
+    bw = torch.linspace(-0.06, 0.06, 1 << nbits, device=device)
+    Qh = make_queries(nqry, nq, d, 7).pin_memory()
+    Qd = Qh.to(device)
+    scorer = tms.ResidualMaxSim(cent, bw, nbits)
+    group = dist.group.WORLD if world > 1 else None
+    score_ev = []
+
+    def step(Q, timed=False):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        s = scorer.score_queries(Q, codes, res, off)
+        e1.record()
+        if timed:
+            score_ev.append((e0, e1))
+        v, i = tms.topk(s, k, id_base=rank * n_docs)
+        return merge_topk(v, i, k, group)
+
+    for _ in range(args.warmup):
+        step(Qd)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(Qd, timed=True)
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    kern_list = [a.elapsed_time(b) for a, b in score_ev]
+    kern_ms = sum(kern_list) / len(kern_list)
+    if world == 1:  # the captured step (see run_ours)
+        from tilemaxsim_b200 import GraphedStep
+        def plain_step(Q):
+            v, i = tms.topk(scorer.score_queries(Q, codes, res, off), k, id_base=rank * n_docs)
+            return merge_topk(v, i, k, group)
+        gstep = GraphedStep(plain_step, Qd)
+        e2e_call = lambda: gstep(Qh)  # noqa: E731
+    else:
+        def e2e_call():
+            v, i = step(Qh.to(device, non_blocking=True))
+            return v.cpu(), i.cpu()
+    e2e_call()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        e2e_call()
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+    t_all = torch.tensor([ms, e2e_ms, kern_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, kern_ms = t_all.tolist()
+    if rank != 0:
+        return
+    pairs = nqry * T * world
+    pk = peaks()
+    # algorithmic bytes per launch: codes + residual rows + offsets + scores (the centroid table,
+    # 16 MB, is read through L2)
+    hbm_bytes = T * (4 + d * nbits // 8) + (n_docs + 1) * 8 + nqry * n_docs * 4
+    clocks = clk.summary()
+    emit_json({
+        "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"{args.config}: residual-compressed corpus, {nqry} queries x {nq} tokens vs "
+                               f"{n_docs} docs x {nd} tokens per GPU (d={d}, nbits={nbits}, {n_cent} centroids, "
+                               f"normalised), top-{k}",
+                   "l2": "codes and residuals larger than L2"},
+        "residual_kernel_ms": kern_ms, "residual_kernel_ms_p50_p95": percentiles(kern_list),
+        # the decoder warps (two per scheduler) are latency-bound: the compressed corpus streams at a
+        # small fraction of HBM bandwidth
+        "roofline": {"bound": "hbm", "achieved": hbm_bytes / (kern_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": hbm_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"], "traffic": None,
+                     "note": "decode-latency bound, not HBM bound"},
+        "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s", "h2d_bytes_per_step": Qh.numel() * 2,
+                "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
+        # packing + the decoder kernel per scoring call, then the top-k (and merge) kernels
+        "gpu_launches": search_launches(nqry, n_docs, k, world, 2) * args.steps,
+        "clocks": clocks})
+
+
 def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     import tilemaxsim_b200 as tms
     from tilemaxsim_b200 import _lib
@@ -547,17 +693,19 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PQ_CONFIGS), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PQ_CONFIGS) + sorted(RES_CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     route_library_output_to_stderr()
     args.warmup = max(3, args.warmup)
-    cfg = CONFIGS.get(args.config) or PQ_CONFIGS[args.config]
+    cfg = CONFIGS.get(args.config) or PQ_CONFIGS.get(args.config) or RES_CONFIGS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         if args.config in PQ_CONFIGS:
             run_reference_pq(args, cfg, rank)
+        elif args.config in RES_CONFIGS:
+            run_reference_res(args, cfg, rank)
         else:
             run_reference(args, cfg, rank)
         return 0
@@ -569,6 +717,8 @@ def main() -> int:
     try:
         if args.config in PQ_CONFIGS:
             run_pq(args, cfg, rank, world, device)
+        elif args.config in RES_CONFIGS:
+            run_res(args, cfg, rank, world, device)
         else:
             run_ours(args, cfg, rank, world, device)
     finally:
