@@ -455,6 +455,8 @@ RES_CONFIGS = {
     # residual-compressed corpus (centroid id + 2-bit residuals, 36 bytes per token)
     "q1_res": (1, 32, 128, 2, 65536, 1_000_000, 128, 100),
     "q5_res": (5, 32, 128, 2, 65536, 1_000_000, 128, 100),
+    # small case for ncu captures (codes + residuals 230 MB, still larger than L2)
+    "q1_res_small": (1, 32, 128, 2, 65536, 50_000, 128, 100),
 }
 
 

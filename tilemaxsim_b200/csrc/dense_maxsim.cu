@@ -193,32 +193,30 @@ __host__ __device__ inline ResLayout residual_layout(int d, int nb) {
 }
 
 // Adds the bucket weights of one 8-dimension unit (its NB residual bytes, little-endian in
-// `bits`) to the unit's centroid values.
+// `bits`) to the unit's centroid values; x[k] holds dimensions 2k and 2k + 1 as an fp32 pair.
 template <int NB>
 __device__ __forceinline__ void residual_unit(const uint4& c, uint32_t bits, const float* table,
-                                              float (&x)[8]) {
+                                              uint64_t (&x)[4]) {
   const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
-    x[2 * k] = f.x;
-    x[2 * k + 1] = f.y;
-  }
+  uint64_t w[4];
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const uint32_t v = (bits >> (8 * b)) & 0xffu;
     if (NB == 1) {
-      const float4 w0 = reinterpret_cast<const float4*>(table)[2 * v];
-      const float4 w1 = reinterpret_cast<const float4*>(table)[2 * v + 1];
-      x[0] += w0.x; x[1] += w0.y; x[2] += w0.z; x[3] += w0.w;
-      x[4] += w1.x; x[5] += w1.y; x[6] += w1.z; x[7] += w1.w;
+      const ulonglong2 w0 = reinterpret_cast<const ulonglong2*>(table)[2 * v];
+      const ulonglong2 w1 = reinterpret_cast<const ulonglong2*>(table)[2 * v + 1];
+      w[0] = w0.x; w[1] = w0.y; w[2] = w1.x; w[3] = w1.y;
     } else if (NB == 2) {
-      const float4 w = reinterpret_cast<const float4*>(table)[v];
-      x[4 * b] += w.x; x[4 * b + 1] += w.y; x[4 * b + 2] += w.z; x[4 * b + 3] += w.w;
+      const ulonglong2 wv = reinterpret_cast<const ulonglong2*>(table)[v];
+      w[2 * b] = wv.x; w[2 * b + 1] = wv.y;
     } else {
-      const float2 w = reinterpret_cast<const float2*>(table)[v];
-      x[2 * b] += w.x; x[2 * b + 1] += w.y;
+      w[b] = reinterpret_cast<const unsigned long long*>(table)[v];
     }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
+    x[k] = f2_add(f2_pack(f.x, f.y), w[k]);
   }
 }
 
@@ -311,7 +309,7 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
       const int r = (NT / 8) * p + tk;
       const uint8_t* crow = slot + r * PITCH;
       const uint8_t* brow = slot + R.bits_off + r * RB;
-      float x[UPP][8];
+      uint64_t x[UPP][4];
 #pragma unroll
       for (int i = 0; i < UPP; ++i) {
         const int u = h + 8 * i;
@@ -324,15 +322,16 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
       }
       float scale = 1.0f;
       if (nrm) {
-        float s0 = 0.0f, s1 = 0.0f;
+        uint64_t s0 = 0ull, s1 = 0ull;  // two pairs of partial sums of squares
 #pragma unroll
         for (int i = 0; i < UPP; ++i)
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            s0 = fmaf(x[i][e], x[i][e], s0);
-            s1 = fmaf(x[i][e + 1], x[i][e + 1], s1);
+          for (int k = 0; k < 4; k += 2) {
+            s0 = f2_fma(x[i][k], x[i][k], s0);
+            s1 = f2_fma(x[i][k + 1], x[i][k + 1], s1);
           }
-        float ss = s0 + s1;
+        const float2 q = f2_unpack(f2_add(s0, s1));
+        float ss = q.x + q.y;
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
         ss += __shfl_xor_sync(0xffffffffu, ss, 2);
         ss += __shfl_xor_sync(0xffffffffu, ss, 4);
@@ -344,11 +343,13 @@ __device__ __forceinline__ void residual_decoders(const DenseArgs& a, uint8_t* s
 #pragma unroll
         for (int i = 0; i < UPP; ++i) {
           const int u = h + 8 * i;
+          const uint64_t sc2 = f2_pack(scale, scale);
           uint32_t pk[4];
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const __half2 hv = __floats2half2_rn(x[i][e] * scale, x[i][e + 1] * scale);
-            pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+          for (int k = 0; k < 4; ++k) {
+            const float2 v = f2_unpack(f2_mul(x[i][k], sc2));
+            const __half2 hv = __floats2half2_rn(v.x, v.y);
+            pk[k] = *reinterpret_cast<const uint32_t*>(&hv);
           }
           *reinterpret_cast<uint4*>(rowp + (u >> 3) * (128 * 128) + (((static_cast<uint32_t>(u) & 7u) ^ sw) << 4)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
