@@ -84,3 +84,23 @@ def test_graphed_step_needs_device_inputs():
         GraphedStep(lambda q: q, torch.zeros(2, 32, 128))
     with pytest.raises(ValueError):
         GraphedStep(lambda: None)
+
+
+def test_residual_scorer_validates_before_any_kernel():
+    """ResidualMaxSim checks nbits, the centroid width, the bucket-weight count and the residual
+    row width on the host, and refuses CPU tensors (no CPU fallback)."""
+    from tilemaxsim_b200 import ResidualMaxSim
+    cent = torch.zeros(16, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="nbits"):
+        ResidualMaxSim(cent, torch.zeros(8), 3)
+    with pytest.raises(ValueError, match="centroids"):
+        ResidualMaxSim(torch.zeros(16, 96, dtype=torch.float16), torch.zeros(4), 2)
+    with pytest.raises(ValueError, match="bucket weights"):
+        ResidualMaxSim(cent, torch.zeros(3), 2)
+    sc = ResidualMaxSim(cent, torch.zeros(4), 2)
+    assert sc.d == 128 and sc.nbits == 2 and sc.centroids.dtype == torch.float16
+    Q = torch.zeros(1, 32, 128, dtype=torch.float16)
+    codes = torch.zeros(10, dtype=torch.int32)
+    res = torch.zeros(10, 32, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="CUDA"):
+        sc.score_queries(Q, codes, res, torch.tensor([0, 10]))
