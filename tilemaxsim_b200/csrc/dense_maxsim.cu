@@ -32,7 +32,9 @@
 //
 // Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
 // warps 2..9 = epilogue (lane quarter = warp % 4). The PQ variant adds warps 10..13, which decode
-// uint8 codes through a shared-memory fp16 codebook into the D stages instead of a TMA load.
+// uint8 codes through a shared-memory fp16 codebook into the D stages instead of a TMA load; the
+// residual variant adds warps 10..17, which rebuild residual-compressed tokens (centroid row +
+// bucket weights, gathered one tile ahead into a shared-memory ring) into the D stages.
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
