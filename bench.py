@@ -323,18 +323,23 @@ def search_launches(rows: int, n: int, k: int, world: int, score_launches: int) 
 
 
 PQ_CONFIGS = {
-    # name: (n_queries, nq, M, K, dsub, n_docs per GPU, nd, k)
+    # name: (n_queries, nq, M, K, dsub, n_docs per GPU, nd, k) -- BASELINE config 4, scored with
+    # the reference's fp32 table arithmetic (TileMaxSimPQ's default, exact=True)
     "c4": (16, 32, 16, 256, 8, 1_000_000, 128, 100),
     "c4_small": (16, 32, 16, 256, 8, 50_000, 128, 100),
     # single-query PQ over the same corpus (the north star's single-query PQ path)
     "q1_pq": (1, 32, 16, 256, 8, 1_000_000, 128, 100),
 }
+# the same workloads on the tensor-core mode (exact=False: codebook rounded to fp16, ~1e-3 relative)
+PQ_CONFIGS.update({f"{k}_fast": v for k, v in list(PQ_CONFIGS.items())})
 
 
-def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int) -> int:
-    """Kernels one default-mode PQ scoring call launches (csrc/pq_adc.cu routing): the token-rows
-    kernel for 1-2 query chunks, else query packing + the decoder-warp dense kernel; plus the chunk
-    sum when Nq > 32."""
+def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> int:
+    """Kernels one PQ scoring call launches (csrc/pq_adc.cu routing). Exact mode: the table-lookup
+    kernel, plus the slice sum when Nq > 8. Fast mode: the token-rows kernel for 1-2 query chunks,
+    else query packing + the decoder-warp dense kernel; plus the chunk sum when Nq > 32."""
+    if exact:
+        return 1 + (1 if nq > 8 else 0)
     chunks = nqry * -(-nq // 32)
     d = M * dsub
     tokrows = chunks <= 2 and d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256
@@ -346,6 +351,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
     import tilemaxsim_b200 as tms
     from tilemaxsim_b200.sharded import merge_topk
     nqry, nq, M, K, dsub, n_docs, nd, k = cfg
+    exact = not args.config.endswith("_fast")
     T = n_docs * nd
     g = torch.Generator(device=device).manual_seed(42 + rank)
     codes = torch.randint(0, K, (T, M), generator=g, device=device, dtype=torch.uint8)
@@ -353,7 +359,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
     cb = torch.randn(M, K, dsub, generator=torch.Generator().manual_seed(42)).to(device)
     Qh = make_queries(nqry, nq, M * dsub, 7).pin_memory()
     Qd = Qh.to(device)
-    pq = tms.TileMaxSimPQ(cb)
+    pq = tms.TileMaxSimPQ(cb, exact=exact)
     group = dist.group.WORLD if world > 1 else None
     score_ev = []
 
@@ -413,40 +419,57 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
     lookups = nqry * nq * T * M  # per GPU per step
     code_bytes = T * M + nqry * n_docs * 4 + M * K * dsub * 4 + nqry * nq * M * dsub * 2
     pk = peaks()
-    flops = 2.0 * nqry * nq * T * M * dsub
-    tmem_bytes = 4.0 * nqry * nq * T
     clocks = clk.summary()
-    tmem_peak = 56.0 * torch.cuda.get_device_properties(device).multi_processor_count * \
-        (ClockSampler.last_sm_mhz or 1965.0) * 1e6 / 1e9
-    gather_bytes = float(T) * M * dsub * 2
-    smem_peak = 128.0 * torch.cuda.get_device_properties(device).multi_processor_count * \
-        (ClockSampler.last_sm_mhz or 1965.0) * 1e6 / 1e9
+    mhz = ClockSampler.last_sm_mhz or 1965.0
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    hbm = {"achieved_gbs": code_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": pk["hbm_gbs"],
+           "frac": code_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+    if exact:
+        # table lookups: one fp32 entry per (query token, doc token, subspace), read from shared
+        # memory; the port moves 128 B per clock per SM = 32 conflict-free 4-byte lookups
+        lk_peak = 32.0 * sms * mhz * 1e6
+        roof = {"bound": "smem", "achieved": lookups / (kern_ms * 1e-3) / 1e9, "peak": lk_peak / 1e9,
+                "unit": "G lookups/s", "frac": lookups / (kern_ms * 1e-3) / lk_peak, "traffic": None,
+                "hbm": hbm,
+                "note": "fp32 table lookups straight from uint8 codes (reference arithmetic); peak = "
+                        "32 lookups/clk/SM (the 128 B/clk shared-memory port) x SMs x median SM clock"}
+    else:
+        flops = 2.0 * nqry * nq * T * M * dsub
+        tmem_bytes = 4.0 * nqry * nq * T
+        tmem_peak = 56.0 * sms * mhz * 1e6 / 1e9
+        gather_bytes = float(T) * M * dsub * 2
+        smem_peak = 128.0 * sms * mhz * 1e6 / 1e9
+        # codes decoded in shared memory, MMA on the tensor cores, the epilogue reading every fp32
+        # similarity from TMEM (B_q*Nq*T values) -- the same bound as the dense kernel
+        roof = {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12,
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": flops / (kern_ms * 1e-3) / 1e12 / pk["bf16_tflops"], "traffic": None,
+                "hbm": hbm,
+                "tmem_read": {"achieved_gbs": tmem_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
+                              "frac": tmem_bytes / (kern_ms * 1e-3) / 1e9 / tmem_peak},
+                # decoding reads one codebook row (dsub fp16) per code from shared memory:
+                # T*M*dsub*2 bytes per launch at least, against 128 B/clk per SM
+                "smem_gather": {"achieved_gbs": gather_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": smem_peak,
+                                "frac": gather_bytes / (kern_ms * 1e-3) / 1e9 / smem_peak},
+                "note": "codebook rounded to fp16 (exact=False); LUT lookups/s counts the table-lookup "
+                        "equivalent (B_q*Nq*T*M) of the work"}
     emit_json({
         "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": f"{args.config}: PQ-ADC, {nqry} queries x {nq} tokens vs {n_docs} docs x {nd} "
-                               f"uint8 codes per GPU (M={M}, K={K}, dsub={dsub}, fp32 codebook), top-{k}",
+                               f"uint8 codes per GPU (M={M}, K={K}, dsub={dsub}, fp32 codebook), top-{k}, "
+                               + ("fp32 table lookups (reference precision)" if exact
+                                  else "tensor-core mode (fp16 codebook)"),
                    "l2": "codes larger than L2"},
         "queries_per_s": nqry / (ms * 1e-3), "pq_kernel_ms": kern_ms,
         "pq_kernel_ms_p50_p95": percentiles(kern_list),
         "lut_lookups_per_s": lookups / (kern_ms * 1e-3),
-        # default path: codes decoded in shared memory, MMA on the tensor cores, the epilogue reading
-        # every fp32 similarity from TMEM (B_q*Nq*T values) -- the same bound as the dense kernel
-        "roofline": {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12,
-                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": flops / (kern_ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], "traffic": None,
-                     "hbm": {"achieved_gbs": code_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": pk["hbm_gbs"]},
-                     "tmem_read": {"achieved_gbs": tmem_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
-                                   "frac": tmem_bytes / (kern_ms * 1e-3) / 1e9 / tmem_peak},
-                     # decoding reads one codebook row (dsub fp16) per code from shared memory:
-                     # T*M*dsub*2 bytes per launch at least, against 128 B/clk per SM
-                     "smem_gather": {"achieved_gbs": gather_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": smem_peak,
-                                     "frac": gather_bytes / (kern_ms * 1e-3) / 1e9 / smem_peak},
-                     "note": "LUT lookups/s counts the table-lookup equivalent (B_q*Nq*T*M) of the work"},
+        "roofline": roof,
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s", "h2d_bytes_per_step": Qh.numel() * 2,
                 "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
-        "gpu_launches": search_launches(nqry, n_docs, k, world, pq_score_launches(nqry, nq, M, K, dsub)) * args.steps,
+        "gpu_launches": search_launches(nqry, n_docs, k, world,
+                                        pq_score_launches(nqry, nq, M, K, dsub, exact)) * args.steps,
         "clocks": clocks})
 
 

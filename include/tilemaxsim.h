@@ -52,8 +52,8 @@ extern "C" {
 #define TMS_F32 2 /* multiplied as TF32 on the tensor cores, like the reference's tl.dot on fp32 */
 
 /* PQ modes */
-#define TMS_PQ_FAST 0  /* tensor cores where the shape allows (default) */
-#define TMS_PQ_EXACT 1 /* fp32 table lookups */
+#define TMS_PQ_FAST 0  /* tensor cores where the shape allows (fp16 codebook) */
+#define TMS_PQ_EXACT 1 /* fp32 table lookups, the reference precision (Python default) */
 
 /* dense output modes */
 #define TMS_OUT_SCORE 0     /* out[q * n_docs + doc] = sum_i max_j <Q_qi, D_j>                 */
@@ -131,8 +131,10 @@ TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, i
  * never written to HBM; |error| <= 1e-3*|score| + 5e-3): up to two 32-row query chunks
  * (n_queries * ceil(nq / 32) <= 2, d <= 256) with the decoded tokens written to tensor memory,
  * larger batches with the tokens decoded into shared memory; other shapes fall back to:
- * mode TMS_PQ_EXACT: the fp32 distance table is built in shared memory and table entries are
- * summed in m order (the reference's arithmetic). The workspace must be 1024-byte aligned. */
+ * mode TMS_PQ_EXACT: the fp32 distance table of eight query tokens is built in shared memory and
+ * table entries are summed straight from the codes (the reference's arithmetic; M = 8 or 16 with
+ * code rows aligned to M bytes take a bank-conflict-free layout that sums the subspaces in groups
+ * of four, other shapes sum in m order). The workspace must be 1024-byte aligned. */
 TMS_API int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int64_t nq,
                           const void* codebook, int cb_dtype, int64_t M, int64_t K, int64_t dsub,
                           const uint8_t* codes, int64_t n_tokens, const int64_t* doc_offsets,

@@ -177,7 +177,7 @@ def test_bounded_wait_reports_timeout(case, cuda_device):
     lib = _lib.load()
     if case.startswith("pq"):
         cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
-        pq = TileMaxSimPQ(cb)
+        pq = TileMaxSimPQ(cb, exact=False)
         codes = torch.randint(0, 256, (40 * 64, 16), generator=R.gen(4), dtype=torch.uint8).to(cuda_device)
         off = (torch.arange(41, dtype=torch.int64) * 64).to(cuda_device)
         # 5 queries: decoder-warp variant of the dense kernel; 1 query: token-rows kernel

@@ -34,12 +34,15 @@ def test_graphed_pq_step_equals_eager(cuda_device):
     lengths = R.ragged_lengths(500, 0, 150, seed=9)
     off = torch.from_numpy(R.offsets_from_lengths(lengths)).to(cuda_device)
     codes = torch.randint(0, 256, (int(off[-1]), 16), generator=R.gen(5), dtype=torch.uint8).to(cuda_device)
-    pq = TileMaxSimPQ(R.randn((16, 256, 8), 3, torch.float32).to(cuda_device))
+    cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
 
-    def fn(Q):
-        return topk(pq.score_queries(Q, codes, off), 20)
+    # token-rows kernel, decoder-warp kernel (exact=False); the table-lookup kernel (default)
+    for nq_, exact in ((1, False), (5, False), (3, True)):
+        pq = TileMaxSimPQ(cb, exact=exact)
 
-    for nq_ in (1, 5):  # token-rows kernel, decoder-warp kernel
+        def fn(Q):
+            return topk(pq.score_queries(Q, codes, off), 20)
+
         q0 = R.normalized((nq_, 32, 128), 4)
         step = GraphedStep(fn, q0.to(cuda_device))
         qh = R.normalized((nq_, 32, 128), 11).pin_memory()

@@ -99,3 +99,31 @@ def test_residual_decompress_bit_order():
     one = O.residual_decompress(np.zeros((1, 8), np.float16), np.array([0]), np.array([[0b10000000]], np.uint8),
                                 np.array([0.0, 1.0], np.float32), 1, normalize=False)
     np.testing.assert_array_equal(one[0], np.array([1, 0, 0, 0, 0, 0, 0, 0], np.float16))
+
+
+def test_exact_f64_scores_and_error_bound():
+    """The float64 scorer matches the fp32 oracle to fp32 rounding; the derived error bound covers
+    the fp32 oracle's own deviation on every (query, document); the ranking check accepts the fp32
+    oracle's top-k and rejects a real inversion."""
+    g = torch.Generator().manual_seed(3)
+    Q = torch.nn.functional.normalize(torch.randn(4, 32, 128, generator=g), dim=-1).half()
+    lengths = R.ragged_lengths(400, 0, 60, 5)
+    off = R.offsets_from_lengths(lengths)
+    D = torch.nn.functional.normalize(torch.randn(int(off[-1]), 128, generator=g), dim=-1).half()
+    exact = O.maxsim_ragged_f64(Q, D, off)
+    f32 = O.maxsim_ragged(Q, D, off)
+    fin = np.isfinite(exact)
+    assert np.array_equal(np.isinf(f32), ~fin) and (~fin).sum() == 4 * (lengths == 0).sum()
+    qn = np.linalg.norm(Q.double().numpy(), axis=-1)
+    bound = O.maxsim_error_bound(qn, O.doc_max_norm(D, off), exact, 128)
+    assert np.all(np.abs(f32[fin] - exact[fin]) <= bound[fin])
+    for r in range(4):
+        _, ids = O.topk(f32[r], 50)
+        O.check_ranking_within_bound(ids, f32[r], exact[r], bound[r], 50)
+    # a top-k that swaps two documents far apart is rejected
+    _, ids = O.topk(f32[0], 50)
+    bad_scores = f32[0].copy()
+    bad_scores[ids[0]], bad_scores[ids[40]] = bad_scores[ids[40]], bad_scores[ids[0]]
+    _, bad_ids = O.topk(bad_scores, 50)
+    with pytest.raises(AssertionError):
+        O.check_ranking_within_bound(bad_ids, bad_scores, exact[0], bound[0], 50)

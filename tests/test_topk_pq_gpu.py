@@ -52,8 +52,9 @@ def test_topk_merge_with_ids(cuda_device):
 
 
 PATHS = ["tensor", "exact"]  # tensor-core decode path (default) / fp32 table-lookup path
-# tensor path: codebook rounded to fp16 -> |error| <= 1e-3*|score| + 5e-3; exact path: 1e-3 + 1e-3
-TOL = {"tensor": (1e-3, 5e-3), "exact": (1e-3, 1e-3)}
+# tensor path (exact=False): codebook rounded to fp16 -> |error| <= 1e-3*|score| + 5e-3
+# exact path (the default): the reference's fp32 table arithmetic, summed in another order
+TOL = {"tensor": (1e-3, 5e-3), "exact": (1e-5, 1e-4)}
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -120,7 +121,7 @@ def test_pq_small_batch_token_rows(nqry, M, K, dsub, nq, lengths, cuda_device):
     cb = R.randn((M, K, dsub), 3, torch.float32)
     Qb = R.normalized((nqry, nq, M * dsub), 4)
     codes = torch.randint(0, K, (int(off[-1]), M), generator=R.gen(5), dtype=torch.uint8)
-    pq = TileMaxSimPQ(cb.to(cuda_device))
+    pq = TileMaxSimPQ(cb.to(cuda_device), exact=False)
     got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device),
                            torch.from_numpy(off).to(cuda_device)).cpu().numpy()
     want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
@@ -139,7 +140,7 @@ def test_pq_offsets_not_starting_at_zero_and_empty_corpus(nqry, cuda_device):
     lens = R.ragged_lengths(300, 0, 150, seed=11)
     off = R.offsets_from_lengths(lens) + 777
     codes = torch.randint(0, 256, (int(off[-1]) + 50, 16), generator=R.gen(5), dtype=torch.uint8)
-    pq = TileMaxSimPQ(cb.to(cuda_device))
+    pq = TileMaxSimPQ(cb.to(cuda_device), exact=False)
     got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device),
                            torch.from_numpy(off).to(cuda_device)).cpu().numpy()
     want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
@@ -162,7 +163,7 @@ def test_pq_fast_mode_rounds_wider_queries_to_fp16(qdtype, nqry, cuda_device):
     cb = R.randn((16, 256, 8), 3, torch.float32)
     Qb = R.normalized((nqry, 32, 128), 4).float().to(qdtype)
     codes = torch.randint(0, 256, (int(off[-1]), 16), generator=R.gen(5), dtype=torch.uint8)
-    got = TileMaxSimPQ(cb.to(cuda_device)).score_queries(
+    got = TileMaxSimPQ(cb.to(cuda_device), exact=False).score_queries(
         Qb.to(cuda_device), codes.to(cuda_device), torch.from_numpy(off).to(cuda_device)).cpu().numpy()
     want = O.pq_maxsim_adc_ragged(Qb.float(), cb, codes, off)
     inf = np.isinf(want)
@@ -180,7 +181,7 @@ def test_pq_single_query_full_size_property(cuda_device):
     off = torch.arange(n + 1, device=cuda_device, dtype=torch.int64) * nd
     cb = torch.randn(16, 256, 8, generator=g, device=cuda_device)
     Q = torch.nn.functional.normalize(torch.randn(1, 32, 128, generator=g, device=cuda_device), dim=-1).half()
-    fast = TileMaxSimPQ(cb).score_queries(Q, codes, off)
+    fast = TileMaxSimPQ(cb, exact=False).score_queries(Q, codes, off)
     exact = TileMaxSimPQ(cb, exact=True).score_queries(Q, codes, off)
     torch.testing.assert_close(fast, exact, rtol=1e-3, atol=5e-3)
 
@@ -195,6 +196,45 @@ def test_pq_tensor_path_full_size_property(cuda_device):
     off = torch.arange(n + 1, device=cuda_device, dtype=torch.int64) * nd
     cb = torch.randn(16, 256, 8, generator=g, device=cuda_device)
     Qb = torch.nn.functional.normalize(torch.randn(16, 32, 128, generator=g, device=cuda_device), dim=-1).half()
-    fast = TileMaxSimPQ(cb).score_queries(Qb, codes, off)
+    fast = TileMaxSimPQ(cb, exact=False).score_queries(Qb, codes, off)
     exact = TileMaxSimPQ(cb, exact=True).score_queries(Qb, codes, off)
     torch.testing.assert_close(fast, exact, rtol=1e-3, atol=5e-3)
+
+
+def test_pq_exact_c4_shape_vs_oracle(cuda_device):
+    """BASELINE config 4 shape (16 queries x 32 tokens, M=16, K=256, dsub=8, 128-token documents,
+    fp32 codebook) on a 1000-document slice: the default (exact) path agrees with the reference's
+    ADC arithmetic within 1e-5 relative."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    g = torch.Generator().manual_seed(12)
+    n, nd = 1000, 128
+    codes = torch.randint(0, 256, (n * nd, 16), generator=g, dtype=torch.uint8)
+    off = np.arange(n + 1, dtype=np.int64) * nd
+    cb = torch.randn(16, 256, 8, generator=g)
+    Qb = torch.nn.functional.normalize(torch.randn(16, 32, 128, generator=g), dim=-1).half()
+    got = TileMaxSimPQ(cb.to(cuda_device)).score_queries(
+        Qb.to(cuda_device), codes.to(cuda_device), torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-4)
+
+
+def test_pq_exact_c4_full_size_document_independence(cuda_device):
+    """BASELINE config 4 at full size (16 queries x 1M documents x 128 codes): the full corpus
+    scored at once equals sampled documents scored alone, bit for bit, and the samples agree with
+    the reference's ADC arithmetic within 1e-5 relative."""
+    from tilemaxsim_b200 import TileMaxSimPQ
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    n, nd = 1_000_000, 128
+    codes = torch.randint(0, 256, (n * nd, 16), generator=g, device=cuda_device, dtype=torch.uint8)
+    off = torch.arange(n + 1, device=cuda_device, dtype=torch.int64) * nd
+    cb = torch.randn(16, 256, 8, generator=g, device=cuda_device)
+    Qb = torch.nn.functional.normalize(torch.randn(16, 32, 128, generator=g, device=cuda_device), dim=-1).half()
+    pq = TileMaxSimPQ(cb)
+    full = pq.score_queries(Qb, codes, off)
+    pick = torch.from_numpy(np.sort(np.random.default_rng(3).choice(n, 200, replace=False))).to(cuda_device)
+    sub_codes = codes.view(n, nd, 16)[pick].reshape(-1, 16)
+    sub_off = torch.arange(201, device=cuda_device, dtype=torch.int64) * nd
+    sub = pq.score_queries(Qb, sub_codes, sub_off)
+    assert torch.equal(full[:, pick], sub)
+    want = O.pq_maxsim_adc_ragged(Qb.cpu(), cb.cpu(), sub_codes.cpu(), sub_off.cpu().numpy())
+    np.testing.assert_allclose(sub.cpu().numpy(), want, rtol=1e-5, atol=1e-4)

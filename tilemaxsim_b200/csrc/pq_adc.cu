@@ -17,6 +17,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "tms_device.cuh"
 #include "tms_internal.h"
 
@@ -155,6 +157,134 @@ __global__ void __launch_bounds__(kPqThreads)
   }
 }
 
+// Bank-conflict-free table lookups (M % 4 == 0, the common shapes M = 8 and 16).
+//
+// The kernel above gives each lane its own document token, so the 32 lanes of a load read table
+// rows chosen by 32 random codes and collide in the shared-memory banks (about 2.4 wavefronts per
+// ideal one at M = 16). Here the lanes of a warp work on the SAME token: lane = (g, i) with
+// i = lane & 7 the query token of the slice and g = lane >> 3 one of four subspace groups
+// (subspaces m = 4a + g, a = 0 .. M/4-1). The table is stored as rows of 32 floats,
+//
+//     T4[a][k][8 g + i] = <Q[q, i0 + i, m-slice], C[m, k]>,   m = 4a + g,
+//
+// so at every step a the four lane groups read four rows picked by four different codes, but each
+// group only ever touches its own eight banks (8 g .. 8 g + 7): every load is one wavefront,
+// whatever the codes are. Each lane sums its M/4 subspaces; four tokens are processed together and
+// a two-round reduce-scatter over the lane groups (3 shuffles) leaves the full sum of token g in
+// lane group g, which keeps a running max over its tokens of the document. At the document's end
+// the groups' maxima are merged (2 shuffles) and the 8 query tokens summed (3 shuffles).
+// Per 4 tokens and 8 query tokens: 4 uniform 16-byte code loads, 4 M/4 table loads and 3 shuffles.
+// The m-summation order is (groups of 4 subspaces, then across groups) instead of the reference's
+// m = 0, 1, 2, ...: the sums differ only by fp32 rounding.
+constexpr int kLut4Threads = 512;
+
+template <int A, int KT>  // A = M / 4 table rows per token; KT = K when it is 256, else 0
+__global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a) {
+  extern __shared__ __align__(128) float tbl4[];  // [A][K][32]
+  const int n_slices = gridDim.x / a.n_doc_parts;
+  // consecutive CTAs share a document range (and its codes in L2) and differ in query slice
+  const int slice_id = blockIdx.x % n_slices;
+  const int part = blockIdx.x / n_slices;
+  const int q = slice_id / a.nslice;
+  const int i0 = (slice_id - q * a.nslice) * 8;
+  const int d = a.M * a.dsub;
+  const int K = KT ? KT : a.K;
+
+  for (int e = threadIdx.x; e < A * K * 32; e += blockDim.x) {
+    const int col = e & 31;
+    const int ak = e >> 5;
+    const int aa = ak / K, k = ak - aa * K;
+    const int m = 4 * aa + (col >> 3);
+    const int i = i0 + (col & 7);
+    float acc = 0.0f;
+    if (i < a.nq) {
+      const int64_t qrow = (static_cast<int64_t>(q) * a.nq + i) * d + m * a.dsub;
+      const int64_t crow = (static_cast<int64_t>(m) * K + k) * a.dsub;
+      for (int t = 0; t < a.dsub; ++t)
+        acc = fmaf(load_elem(a.Q, a.q_dtype, qrow + t), load_elem(a.cb, a.cb_dtype, crow + t), acc);
+    }
+    tbl4[e] = acc;
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 3, i = lane & 7;
+  const int n_warps = blockDim.x >> 5;
+  const int64_t n_docs = a.docs.n_docs;
+  const int64_t doc_begin = n_docs * part / a.n_doc_parts;
+  const int64_t doc_end = n_docs * (part + 1) / a.n_doc_parts;
+  const int ns = min(8, a.nq - i0);
+  const uint32_t kmax = static_cast<uint32_t>(K - 1);
+  // Byte g of a code word, scaled to the 128-byte table row and or-ed with this lane's column:
+  // a funnel rotate brings bits [8g, 8g + 8) to [7, 15), one 3-input logic op masks them and
+  // inserts lane * 4 (bits 0-6, zero after the mask).
+  const uint32_t rot = static_cast<uint32_t>(8 * g - 7) & 31u;
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+  auto row_off = [&](uint32_t w) -> uint32_t {
+    if constexpr (KT == 256) {
+      return (__funnelshift_r(w, w, rot) & 0x7f80u) | lane4;
+    } else {
+      const uint32_t code = min((w >> (8 * g)) & 0xffu, kmax);  // a code >= K never reads past the table
+      return (code << 7) | lane4;
+    }
+  };
+  const char* tb = reinterpret_cast<const char*>(tbl4);
+  auto lookup = [&](int aa, uint32_t off) -> float {
+    return *reinterpret_cast<const float*>(tb + static_cast<uint32_t>(aa * K * 128) + off);
+  };
+  using CodeVec = typename std::conditional<A == 4, uint4, uint2>::type;
+  auto word = [](const CodeVec& c, int aa) -> uint32_t {
+    if constexpr (A == 4) return aa == 0 ? c.x : aa == 1 ? c.y : aa == 2 ? c.z : c.w;
+    else return aa == 0 ? c.x : c.y;
+  };
+
+  for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
+    // clamped to the code rows that exist, so malformed offsets never read outside `codes`
+    const int64_t t_lo = max(min(a.docs.start(doc), a.n_tokens), int64_t(0));
+    const int64_t t_hi = max(min(a.docs.start(doc + 1), a.n_tokens), t_lo);
+    const int len = static_cast<int>(min(t_hi - t_lo, int64_t(0x7fffffff)));
+    const CodeVec* rows = reinterpret_cast<const CodeVec*>(a.codes) + t_lo;
+    float run = kNegInfPq;
+    // Lane group g handles the four tokens of a step in the order j0 + (t ^ g): after the
+    // reduce-scatter below its own token j0 + g then needs no select.
+    auto load4 = [&](int j0, CodeVec (&c)[4]) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) c[t] = __ldg(rows + min(j0 + (t ^ g), len - 1));
+    };
+    if (len > 0) {
+      CodeVec nxt[4];
+      load4(0, nxt);
+      for (int j0 = 0; j0 < len; j0 += 4) {
+        CodeVec cur[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) cur[t] = nxt[t];
+        load4(j0 + 4, nxt);  // the next four tokens' codes in flight
+        float p[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float acc = lookup(0, row_off(word(cur[t], 0)));
+#pragma unroll
+          for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(word(cur[t], aa)));
+          p[t] = acc;  // token j0 + (t ^ g), this lane's subspaces
+        }
+        // reduce-scatter over the lane groups: the partner g ^ 2 holds tokens j0 + g (its t = 2)
+        // and j0 + (1 ^ g) (its t = 3); then g ^ 1 holds j0 + g as its t = 1
+        const float q0 = p[0] + __shfl_xor_sync(0xffffffffu, p[2], 16);
+        const float q1 = p[1] + __shfl_xor_sync(0xffffffffu, p[3], 16);
+        const float sum = q0 + __shfl_xor_sync(0xffffffffu, q1, 8);
+        if (j0 + g < len) run = fmaxf(run, sum);
+      }
+    }
+    run = fmaxf(run, __shfl_xor_sync(0xffffffffu, run, 8));
+    run = fmaxf(run, __shfl_xor_sync(0xffffffffu, run, 16));
+    float tot = (i < ns) ? run : 0.0f;
+    tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 4);
+    if (lane == 0) a.out[static_cast<int64_t>(slice_id) * n_docs + doc] = tot;
+  }
+}
+
 __global__ void pq_sum_slices_kernel(const float* __restrict__ partial, float* __restrict__ out,
                                      int64_t n_queries, int64_t n_docs, int nslice) {
   const int64_t total = n_queries * n_docs;
@@ -270,11 +400,14 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
                                  st);
     if (rc != TMS_ERR_UNSUPPORTED) return rc;
   }
-  const int qs = pick_qs(M, K, nq);
-  const size_t smem = static_cast<size_t>(M * K * qs) * 4;
+  // conflict-free lookups for M = 8 / 16 (code rows aligned to their size), else the general kernel
+  const bool lut4 = (M == 16 || M == 8) && (reinterpret_cast<uintptr_t>(codes) % M) == 0 &&
+                    M * K * 32 <= kPqTableBudget;
+  const int qs = lut4 ? 8 : pick_qs(M, K, nq);
+  const size_t smem = static_cast<size_t>(M * K * (lut4 ? 32 : qs)) * (lut4 ? 1 : 4);
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
   const int nslice = static_cast<int>((nq + qs - 1) / qs);
-  const size_t need = pq_lut_workspace_size(n_queries, nq, M, K, n_docs);
+  const size_t need = nslice > 1 ? static_cast<size_t>(n_queries * nslice * n_docs) * 4 : 0;
   if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
   const bool m16 = (M == 16) && ((reinterpret_cast<uintptr_t>(codes) & 15) == 0);
 
@@ -296,6 +429,13 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   a.nslice = nslice;
   const int64_t slices = n_queries * nslice;
   int64_t parts = (2LL * dev->num_sms + slices - 1) / slices;
+  if (lut4) {
+    // one 512-thread CTA per SM: the fewest document parts that make slices x parts a whole
+    // number of waves (gcd rule)
+    int64_t gcd = dev->num_sms, gb = slices;
+    while (gb) { const int64_t t = gcd % gb; gcd = gb; gb = t; }
+    parts = dev->num_sms / gcd;
+  }
   const int64_t max_parts = (n_docs + 15) / 16;  // at least ~16 docs per CTA
   if (parts > max_parts) parts = max_parts;
   if (parts < 1) parts = 1;
@@ -303,7 +443,15 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   a.n_doc_parts = static_cast<int>(parts);
   const unsigned grid = static_cast<unsigned>(slices * parts);
   int rc;
-  switch (qs) {
+  if (lut4) {
+    auto k = (M == 16) ? (K == 256 ? pq_lut4_kernel<4, 256> : pq_lut4_kernel<4, 0>)
+                       : (K == 256 ? pq_lut4_kernel<2, 256> : pq_lut4_kernel<2, 0>);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return TMS_ERR_CUDA;
+    k<<<grid, kLut4Threads, smem, st>>>(a);
+    rc = cuda_status(cudaGetLastError());
+  } else switch (qs) {
     case 8: rc = launch_pq_t<8>(a, m16, grid, smem, st); break;
     case 4: rc = launch_pq_t<4>(a, m16, grid, smem, st); break;
     case 2: rc = launch_pq_t<2>(a, m16, grid, smem, st); break;

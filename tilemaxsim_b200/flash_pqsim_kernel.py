@@ -4,13 +4,15 @@
 methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_pqsim_kernel.py:
 176-280). Scoring goes through the C ABI ``tms_pq_maxsim`` and reads the uint8 codes directly:
 neither the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote
-both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default the
-queries run on the tensor cores in fp16 (fp32 / bf16 ones are rounded to fp16), each token rebuilt
-on chip from an fp16 copy of the codebook: for one or two 32-row query chunks the rebuilt tokens go
-to tensor memory as the MMA's A operand (token-rows kernel), for larger batches into the dense
-kernel's shared-memory operand tiles.
-``exact=True`` (and any shape the tensor path does not take) uses the table-lookup kernel: each
-CTA builds its query slice's fp32 distance table in shared memory, the reference's arithmetic.
+both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default
+(``exact=True``) scoring keeps the reference's arithmetic: each CTA builds an fp32 distance table
+for eight query tokens in shared memory and sums table entries straight from the uint8 codes (no
+reconstruction), agreeing with the reference's ADC path to fp32 rounding (1e-5 relative).
+``exact=False`` is the faster tensor-core mode: queries in fp16 (fp32 / bf16 ones are rounded to
+fp16) and each token rebuilt on chip from an fp16 copy of the codebook; for one or two 32-row query
+chunks the rebuilt tokens go to tensor memory as the MMA's A operand (token-rows kernel), for
+larger batches into the dense kernel's shared-memory operand tiles. Rounding the codebook to fp16
+costs about 1e-3 relative (|error| <= 1e-3*|score| + 5e-3).
 ``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
 """
 from __future__ import annotations
@@ -32,14 +34,14 @@ def _codes_u8(codes: torch.Tensor) -> torch.Tensor:
 class TileMaxSimPQ:
     """MaxSim over product-quantized documents (reference: src/flash_pqsim_kernel.py:176-280)."""
 
-    def __init__(self, codebook: torch.Tensor, exact: bool = False):
+    def __init__(self, codebook: torch.Tensor, exact: bool = True):
         """codebook: (M, K, dsub) centroids (fp16, bf16 or fp32), K <= 256.
 
-        exact=False (default): queries of a supported shape are scored on the tensor cores in
-        fp16 (fp32 / bf16 queries are rounded to fp16), codes decoded on chip through the
-        codebook rounded to fp16 (|error| <= 1e-3*|score| + 5e-3). exact=True: fp32 table
-        lookups, the reference's arithmetic (also used automatically for shapes the tensor path
-        does not take)."""
+        exact=True (default): fp32 table lookups, the reference's arithmetic (scores within fp32
+        rounding of the reference's ADC path). exact=False: queries of a supported shape are
+        scored on the tensor cores in fp16 (fp32 / bf16 queries are rounded to fp16), codes decoded
+        on chip through the codebook rounded to fp16 (|error| <= 1e-3*|score| + 5e-3); other shapes
+        fall back to the table lookups."""
         self.exact = bool(exact)
         self.codebook = codebook.contiguous()
         self.M, self.K, self.dsub = codebook.shape
