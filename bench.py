@@ -133,66 +133,86 @@ def make_queries(nqry: int, nq: int, d: int, seed: int) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------ arms
-def cpu_baseline(cfg, seconds: float = 12.0) -> dict:
-    """The reference algorithm (oracle port, NumPy fp32 einsum -> max -> sum, all host cores) on a
-    bounded sample: 1 query against the first documents of the shard."""
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _cpu_sample(cfg, n_s: int):
+    """A bounded sample of the workload for the host CPU: 1 query x the first n_s ragged documents
+    (same length distribution), padded in chunks as the reference's CPU scorers take them."""
     from oracle import maxsim_oracle as O
     nqry, nq, d, n_docs, lo, hi, k = cfg
-    n_s = min(n_docs, 5000)
+    n_s = min(n_docs, n_s)
     lengths = np.random.default_rng(42).integers(lo, hi + 1, n_s).astype(np.int64)
     off = np.zeros(n_s + 1, np.int64)
     np.cumsum(lengths, out=off[1:])
-    rng = np.random.default_rng(1)
-    D = rng.standard_normal((int(off[-1]), d), dtype=np.float32)
-    D /= np.linalg.norm(D, axis=1, keepdims=True)
-    D = D.astype(np.float16)
-    Q = make_queries(1, nq, d, 42)[0]
-    O.maxsim_ragged(Q, D, off)  # warm-up
+    g = torch.Generator().manual_seed(1)
+    D = torch.nn.functional.normalize(torch.randn(int(off[-1]), d, generator=g), dim=-1).half()
+    Q = make_queries(1, nq, d, 42)
+    return Q, O.pad_chunks_torch(D, off), n_s, int(off[-1])
+
+
+def _cpu_threads() -> int:
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_baseline(cfg, seconds: float = 12.0) -> dict:
+    """The reference's CPU scoring (torch fp32 einsum -> masked max -> sum, all host cores) on a
+    bounded sample: 1 query against the first documents of the shard."""
+    from oracle import maxsim_oracle as O
+    threads = _cpu_threads()
+    Q, chunks, n_s, T = _cpu_sample(cfg, 5000)
+    O.maxsim_padded_chunks_torch(Q, chunks, n_s)  # warm-up
     t0 = time.perf_counter()
     reps = 0
     while True:
-        O.maxsim_ragged(Q, D, off)
+        O.maxsim_padded_chunks_torch(Q, chunks, n_s)
         reps += 1
         if time.perf_counter() - t0 > seconds:
             break
     dt = (time.perf_counter() - t0) / reps
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    return {"value": reps and int(off[-1]) / dt, "unit": "doc-tokens/s", "cores": cores, "kind": "port",
-            "sample": f"1 query x {n_s} ragged docs ({int(off[-1])} tokens, d={d}) x {reps} reps, "
-                      f"NumPy fp32 restatement of pytorch_maxsim_naive (oracle/maxsim_oracle.py)"}
+    return {"value": T / dt, "unit": "doc-tokens/s", "cores": threads, "kind": "port",
+            "cpu": cpu_model(), "torch_threads": threads,
+            "sample": f"1 query x {n_s} ragged docs ({T} tokens, d={cfg[2]}) x {reps} reps, the reference's "
+                      "pytorch_maxsim_score / pytorch_maxsim_naive arithmetic in torch fp32 on padded chunks "
+                      "of 4096 docs (oracle/maxsim_oracle.py:maxsim_padded_chunks_torch)"}
 
 
 def run_reference(args, cfg, rank: int) -> None:
     if rank != 0:
         return
     from oracle import maxsim_oracle as O
+    threads = _cpu_threads()
     nqry, nq, d, n_docs, lo, hi, k = cfg
-    n_s = min(n_docs, 3000)
-    lengths = np.random.default_rng(42).integers(lo, hi + 1, n_s).astype(np.int64)
-    off = np.zeros(n_s + 1, np.int64)
-    np.cumsum(lengths, out=off[1:])
-    rng = np.random.default_rng(1)
-    D = rng.standard_normal((int(off[-1]), d), dtype=np.float32)
-    D = (D / np.linalg.norm(D, axis=1, keepdims=True)).astype(np.float16)
-    Q = make_queries(1, nq, d, 42)[0]
+    Q, chunks, n_s, T = _cpu_sample(cfg, 3000)
+    kk = min(k, n_s)
     for _ in range(args.warmup):
-        s = O.maxsim_ragged(Q, D, off)
-        O.topk(s, min(k, n_s))
+        torch.topk(O.maxsim_padded_chunks_torch(Q, chunks, n_s), kk)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        s = O.maxsim_ragged(Q, D, off)
-        O.topk(s, min(k, n_s))
+        torch.topk(O.maxsim_padded_chunks_torch(Q, chunks, n_s), kk)
     dt = (time.perf_counter() - t0) / args.steps
-    val = int(off[-1]) / dt
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    sample = (f"per step 1 query x {n_s} ragged docs ({int(off[-1])} tokens, d={d}) + top-{min(k, n_s)}, "
-              "NumPy fp32 restatement of the reference's pytorch_maxsim_naive on all host cores")
+    val = T / dt
+    sample = (f"per step 1 query x {n_s} ragged docs ({T} tokens, d={d}) + torch.topk {kk}, the reference's "
+              "torch fp32 CPU scoring (pytorch_maxsim_score on padded chunks) on all host cores")
     emit_json({
         "impl": "reference", "metric": "doc-tokens scored/s", "value": val, "unit": "doc-tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args, cfg),
-        "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "config": {"workload": f"{args.config} slice: 1 query x {nq} tokens vs {n_s} ragged docs "
+                               f"(N_d ~ U[{lo},{hi}], d={d}), top-{kk}; the full config is {nqry} queries x "
+                               f"{n_docs} docs per GPU", "n_queries": 1, "nq": nq, "d": d, "docs": n_s,
+                   "nd_range": [lo, hi], "k": kk},
+        "cpu_baseline": {"value": val, "unit": "doc-tokens/s", "cores": threads, "kind": "port",
+                         "cpu": cpu_model(), "torch_threads": threads, "sample": sample},
         "e2e": {"value": val, "unit": "doc-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0})
 
@@ -346,7 +366,7 @@ def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool
     return (1 if tokrows else 2) + (1 if nq > 32 else 0)
 
 
-def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
+def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = True) -> dict | None:
     """PQ-ADC scoring (TileMaxSimPQ.score_queries) + per-query top-k over uint8 codes."""
     import tilemaxsim_b200 as tms
     from tilemaxsim_b200.sharded import merge_topk
@@ -453,7 +473,7 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
                                 "frac": gather_bytes / (kern_ms * 1e-3) / 1e9 / smem_peak},
                 "note": "codebook rounded to fp16 (exact=False); LUT lookups/s counts the table-lookup "
                         "equivalent (B_q*Nq*T*M) of the work"}
-    emit_json({
+    out = {
         "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
@@ -470,7 +490,10 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device) -> None:
                 "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
         "gpu_launches": search_launches(nqry, n_docs, k, world,
                                         pq_score_launches(nqry, nq, M, K, dsub, exact)) * args.steps,
-        "clocks": clocks})
+        "clocks": clocks}
+    if emit:
+        emit_json(out)
+    return out
 
 
 RES_CONFIGS = {
@@ -579,7 +602,7 @@ def run_res(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "clocks": clocks})
 
 
-def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
+def run_ours(args, cfg, rank: int, world: int, device: torch.device, emit: bool = True) -> dict | None:
     import tilemaxsim_b200 as tms
     from tilemaxsim_b200 import _lib
     from tilemaxsim_b200.sharded import ShardedIndex
@@ -648,7 +671,11 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
 
     t_all = torch.tensor([ms, e2e_ms, dense_ms, float(T)], dtype=torch.float64, device=device)
+    per_rank = [t_all.tolist()]
     if world > 1:
+        g_all = torch.empty(world, 4, dtype=torch.float64, device=device)
+        dist.all_gather_into_tensor(g_all, t_all)
+        per_rank = g_all.tolist()
         mx = t_all.clone()
         dist.all_reduce(mx[:3], op=dist.ReduceOp.MAX)
         tot = t_all[3:].clone()
@@ -667,12 +694,12 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
     tensor_bound = nqry * nq >= 256
     if tensor_bound:
         ach = flops_launch / (dense_ms * 1e-3) / 1e12
-        peak, unit = pk["bf16_tflops_sustained"], "TFLOP/s"
+        peak, unit = pk["bf16_tflops"], "TFLOP/s"  # burst: an ~11 ms launch in a sub-second loop
     else:
         ach = bytes_launch / (dense_ms * 1e-3) / 1e9
         peak, unit = pk["hbm_gbs"], "GB/s"
     # The epilogue reads every fp32 similarity once from TMEM: B_q*Nq*T values per launch. TMEM ->
-    # register bandwidth measured at ~56 B/clk per SM (tilemaxsim_b200/microbench/tmem_read.cu).
+    # register bandwidth measured at ~56 B/clk per SM with a tcgen05.ld microbenchmark.
     tmem_bytes = 4.0 * nqry * nq * (T_total / world)
     clk = ClockSampler.last_sm_mhz or 1965.0
     tmem_peak = 56.0 * torch.cuda.get_device_properties(device).multi_processor_count * clk * 1e6 / 1e9
@@ -691,25 +718,58 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device) -> None:
         "corpus_tokens_per_s": T_total / (ms * 1e-3),
         "dense_kernel_ms": dense_ms,
         "dense_kernel_ms_p50_p95": percentiles(dense_list),
+        # per rank: (step ms, scoring kernel ms); the slowest rank sets the step time
+        "per_rank_ms": [{"step": r[0], "kernel": r[2]} for r in per_rank],
         "dense_hbm_gbs": bytes_launch / (dense_ms * 1e-3) / 1e9,
         "dense_tflops": flops_launch / (dense_ms * 1e-3) / 1e12,
         "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": ach, "peak": peak, "unit": unit,
                      "frac": ach / peak, "traffic": traffic,
-                     "peak_src": f"{pk['src']} ({'bf16_tflops_sustained' if tensor_bound else 'hbm_gbs'})",
+                     "peak_src": f"{pk['src']} ({'bf16_tflops' if tensor_bound else 'hbm_gbs'})",
                      "algorithmic": {"flops_per_launch": flops_launch, "bytes_per_launch": bytes_launch},
                      "tmem_read": {"achieved_gbs": tmem_bytes / (dense_ms * 1e-3) / 1e9, "peak_gbs": tmem_peak,
                                    "frac": tmem_bytes / (dense_ms * 1e-3) / 1e9 / tmem_peak,
                                    "note": "epilogue reads B_q*Nq*T fp32 values from TMEM; peak = 56 B/clk/SM ("
-                                           "measured by tilemaxsim_b200/microbench/tmem_read.cu) x SMs x median SM clock"}},
+                                           "tcgen05.ld microbenchmark) x SMs x median SM clock"}},
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s",
                 "h2d_bytes_per_step": Qh.numel() * Qh.element_size(),
                 "d2h_bytes_per_step": nqry * k * (4 + 8), "ms_per_step": e2e_ms},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if emit and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg)
-    emit_json(out)
+    if emit and world == 1 and args.config == "c2" and not args.no_legs:
+        out["legs"] = run_legs(args, device)
+    if emit:
+        emit_json(out)
+    return out
+
+
+LEGS = ("q1_ragged", "c3_768", "c4")
+LEG_KEYS = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "roofline", "e2e", "clocks",
+            "dense_kernel_ms", "pq_kernel_ms", "queries_per_s", "gpu_launches")
+
+
+def run_legs(args, device: torch.device) -> dict:
+    """The north star's other single-GPU targets, measured in the same run as the headline line:
+    single-query dense over 400k ragged docs (HBM-bound), the d = 768 sweep (config 3) and PQ at
+    the reference's precision (config 4). Each leg has its own timing, roofline and clock record."""
+    legs = {}
+    for name in LEGS:
+        sub = argparse.Namespace(**vars(args))
+        sub.config = name
+        sub.steps = min(args.steps, 10)
+        sub.warmup = 3
+        torch.cuda.empty_cache()
+        if name in PQ_CONFIGS:
+            r = run_pq(sub, PQ_CONFIGS[name], 0, 1, device, emit=False)
+        else:
+            r = run_ours(sub, CONFIGS[name], 0, 1, device, emit=False)
+        legs[name] = {k: r[k] for k in LEG_KEYS if k in r}
+        legs[name]["steps"] = sub.steps
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return legs
 
 
 def main() -> int:
@@ -720,6 +780,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PQ_CONFIGS) + sorted(RES_CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-legs", action="store_true",
+                    help="c2 on one GPU: skip the single-query, d=768 and PQ legs")
     args = ap.parse_args()
     route_library_output_to_stderr()
     args.warmup = max(3, args.warmup)

@@ -104,9 +104,10 @@ TMS_API int tms_dense_maxsim(const void* Q, int dtype, int64_t n_queries, int64_
  * scratch lives in a fixed 4 MiB static device array that every GPU loading the library holds
  * until exit. Same arguments and results as tms_dense_maxsim without the workspace; returns
  * TMS_ERR_TOO_LARGE when tms_dense_workspace_size() for the problem exceeds 4 MiB (e.g. more than
- * 512 queries of <= 32 tokens at d = 128 fp16). The first call on each device looks up the array's
- * device address (cudaGetSymbolAddress, with that device current) and caches it: make that first
- * call before any stream capture. All calls share the one array, so two calls whose kernels
+ * 512 queries of <= 32 tokens at d = 128 fp16). The first call on each device (and again in each
+ * new CUDA context on it, e.g. after cudaDeviceReset) looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and caches it: make that first call before any
+ * stream capture. All calls share the one array, so two calls whose kernels
  * overlap on the GPU race with each other; issue them on one stream (or otherwise order them).
  * Nothing in the array has to start at zero. It allocates nothing and calls no allocator. */
 TMS_API int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_queries, int64_t nq,

@@ -127,3 +127,41 @@ def test_exact_f64_scores_and_error_bound():
     _, bad_ids = O.topk(bad_scores, 50)
     with pytest.raises(AssertionError):
         O.check_ranking_within_bound(bad_ids, bad_scores, exact[0], bound[0], 50)
+
+
+def _encoded_corpus(nbits: int, d: int = 128, T: int = 3000, n_cent: int = 64, seed: int = 0):
+    import colbert_codec as CC
+    rng = np.random.default_rng(seed)
+    C = rng.standard_normal((n_cent, d)).astype(np.float32)
+    C /= np.linalg.norm(C, axis=1, keepdims=True)
+    # embeddings near the centroids, as after k-means: centroid + small noise, unit length
+    X = C[rng.integers(0, n_cent, T)] + 0.05 * rng.standard_normal((T, d)).astype(np.float32)
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    codes = np.argmax(X @ C.T, axis=1)
+    cut, w = CC.train_buckets(X - C[codes], nbits)
+    codes, packed = CC.compress(X, C, cut, nbits)
+    return X, C, codes, packed, cut, w
+
+
+@pytest.mark.parametrize("nbits", [1, 2, 4])
+def test_residual_layout_matches_colbert_encoder(nbits):
+    """Pins the residual bit layout to a restatement of ColBERTv2's encoder (bucketize, bits spread
+    least-significant first, np.packbits): decoding with weights w[b] = b returns exactly the bucket
+    index the encoder chose for every dimension; with the trained weights the decoded vectors are
+    within the codec's quantisation error of the encoder's inputs."""
+    import colbert_codec as CC
+    X, C, codes, packed, cut, w = _encoded_corpus(nbits)
+    resid = X - C[codes]
+    b = np.searchsorted(cut, resid, side="left")
+    ident = np.arange(1 << nbits, dtype=np.float32)
+    dec = O.residual_decompress(np.zeros_like(C, dtype=np.float16), codes, packed, ident, nbits, normalize=False)
+    np.testing.assert_array_equal(dec.astype(np.int64), b)
+    # quantisation error: inner buckets are bounded by their cutoffs, outer ones by the data range
+    edges = np.concatenate([[resid.min()], cut, [resid.max()]])
+    half = np.maximum(np.abs(w - edges[:-1]), np.abs(edges[1:] - w))  # per bucket
+    raw = O.residual_decompress(C.astype(np.float16), codes, packed, w, nbits, normalize=False).astype(np.float32)
+    tol = half[b] + 2e-3  # + fp16 rounding of the centroid and of the result
+    assert np.all(np.abs(raw - X) <= tol)
+    unit = O.residual_decompress(C.astype(np.float16), codes, packed, w, nbits, normalize=True).astype(np.float32)
+    cos = (unit * X).sum(axis=1)
+    assert cos.min() > 0.9

@@ -84,3 +84,39 @@ def test_residual_long_ranges_and_copy_widths(d, nbits, misalign, cuda_device):
     inf = np.isinf(want)
     np.testing.assert_array_equal(got[inf], want[inf])
     np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("nbits", [1, 2, 4])
+def test_residual_colbert_encoded_corpus(nbits, cuda_device):
+    """End to end from a restatement of ColBERTv2's encoder: seeded embeddings near their centroids
+    are compressed (nearest centroid, quantile buckets, bits least-significant first, packbits),
+    scored on the GPU straight from the compressed form, and checked (a) against the oracle's
+    decompress-then-score to 1e-3 and (b) against MaxSim over the original embeddings to the
+    codec's quantisation error: |score(decoded) - score(X)| <= sum_i |q_i| * max_j |decoded_j - x_j|."""
+    import colbert_codec as CC
+    from tilemaxsim_b200 import ResidualMaxSim
+    rng = np.random.default_rng(nbits)
+    d, n_cent, n_docs = 128, 256, 300
+    C = rng.standard_normal((n_cent, d)).astype(np.float32)
+    C /= np.linalg.norm(C, axis=1, keepdims=True)
+    lens = R.ragged_lengths(n_docs, 1, 120, seed=nbits)
+    off = R.offsets_from_lengths(lens)
+    T = int(off[-1])
+    X = C[rng.integers(0, n_cent, T)] + 0.05 * rng.standard_normal((T, d)).astype(np.float32)
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    codes = np.argmax(X @ C.T, axis=1)
+    cut, w = CC.train_buckets(X - C[codes], nbits)
+    codes, packed = CC.compress(X, C, cut, nbits)
+    cent = torch.from_numpy(C).half()
+    Q = R.normalized((3, 32, d), 9)
+    scorer = ResidualMaxSim(cent.to(cuda_device), torch.from_numpy(w).to(cuda_device), nbits, True)
+    got = scorer.score_queries(Q.to(cuda_device), torch.from_numpy(codes).to(cuda_device),
+                               torch.from_numpy(packed).to(cuda_device),
+                               torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    dec = O.residual_decompress(cent, codes, packed, w, nbits, normalize=True)
+    np.testing.assert_allclose(got, O.maxsim_ragged(Q, torch.from_numpy(dec), off), rtol=1e-3, atol=1e-3)
+    err = np.linalg.norm(dec.astype(np.float32) - X, axis=1)  # per token
+    per_doc = np.maximum.reduceat(err, off[:-1])
+    bound = torch.linalg.vector_norm(Q.float(), dim=-1).sum(-1).numpy()[:, None] * per_doc[None, :]
+    exact = O.maxsim_ragged(Q, torch.from_numpy(X), off)
+    assert np.all(np.abs(got - exact) <= bound + 1e-3)

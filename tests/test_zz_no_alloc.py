@@ -54,6 +54,41 @@ def test_noalloc_matches_workspace_entry_point_twice(n_queries, nq, seed, cuda_d
     assert not np.array_equal(results[0], results[1])
 
 
+def test_noalloc_token_max_matches_workspace_entry_point(cuda_device):
+    """Per-query-token maxima (TMS_OUT_TOKEN_MAX) go through the same static scratch."""
+    from tilemaxsim_b200 import _lib, maxsim_batched
+    lib = _lib.load()
+    for call in range(2):
+        c = R.ragged_case(n_queries=2, nq=40, n_docs=120, seed=61 + call)
+        Qb, D, off = c["Qb"].to(cuda_device), c["D"].to(cuda_device), c["offsets"].to(cuda_device)
+        out = torch.full((2, off.numel() - 1, 40), float("nan"), dtype=torch.float32, device=cuda_device)
+        rc = _noalloc(lib, Qb, D, off, _lib.TMS_OUT_TOKEN_MAX, out)
+        assert rc == _lib.TMS_OK, _lib.strerror(rc)
+        want = maxsim_batched(Qb, D, off, out_mode=_lib.TMS_OUT_TOKEN_MAX).cpu().numpy()
+        got = out.cpu().numpy()
+        inf = np.isinf(want)
+        np.testing.assert_array_equal(got[inf], want[inf])
+        np.testing.assert_allclose(got[~inf], want[~inf], rtol=RTOL, atol=ATOL)
+
+
+def test_noalloc_limit_boundary(cuda_device):
+    """The documented limit: 512 queries of 32 tokens at d = 128 fp16 pack into exactly 4 MiB and
+    run; 513 do not fit and are rejected before any launch."""
+    from tilemaxsim_b200 import _lib
+    lib = _lib.load()
+    D = R.normalized((64, 128), 5).to(cuda_device)
+    off = torch.tensor([0, 30, 64], dtype=torch.int64, device=cuda_device)
+    assert lib.tms_dense_workspace_size(_lib.TMS_F16, 512, 32, 128, 2, _lib.TMS_OUT_SCORE) == 4 << 20
+    Qb = R.normalized((512, 32, 128), 6).to(cuda_device)
+    out = torch.zeros(512, 2, dtype=torch.float32, device=cuda_device)
+    assert _noalloc(lib, Qb, D, off, _lib.TMS_OUT_SCORE, out) == _lib.TMS_OK
+    from tilemaxsim_b200 import maxsim_batched
+    np.testing.assert_allclose(out.cpu().numpy(), maxsim_batched(Qb, D, off).cpu().numpy(), rtol=RTOL, atol=ATOL)
+    Qb = R.normalized((513, 32, 128), 6).to(cuda_device)
+    out = torch.zeros(513, 2, dtype=torch.float32, device=cuda_device)
+    assert _noalloc(lib, Qb, D, off, _lib.TMS_OUT_SCORE, out) == _lib.TMS_ERR_TOO_LARGE
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda_device):
     from tilemaxsim_b200 import _lib
     lib = _lib.load()

@@ -74,8 +74,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    # TMS_LIB_PATH: load another build of the library (A/B benchmarking of kernel variants)
-    p = Path(path) if path is not None else Path(os.environ.get("TMS_LIB_PATH", LIB_PATH))
+    p = Path(path) if path is not None else LIB_PATH
     if not p.exists():
         raise ImportError(
             f"{p} is missing: build it with `python -m tilemaxsim_b200.build` (nvcc, sm_100a). "

@@ -40,7 +40,29 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn get_ctx_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
 }  // namespace
+
+void* current_cu_context() {
+  CUcontext c = nullptr;
+  const CtxGetCurrentFn fn = get_ctx_fn();
+  if (fn) fn(&c);
+  return c;
+}
 
 const DeviceInfo* current_device_info(int* status) {
   int dev = -1;
@@ -48,11 +70,15 @@ const DeviceInfo* current_device_info(int* status) {
     *status = TMS_ERR_CUDA;
     return nullptr;
   }
+  // The cached error-word address belongs to the context the module was loaded in: a different
+  // current context (after cudaDeviceReset, or a caller's own driver context) looks it up again.
+  void* ctx = current_cu_context();
   std::lock_guard<std::mutex> lock(g_dev_mutex);
   DeviceInfo& d = g_devices[dev];
-  if (d.device != dev) {
+  if (d.device != dev || d.ctx != ctx) {
     DeviceInfo n;
     n.device = dev;
+    n.ctx = ctx;
     if (cudaDeviceGetAttribute(&n.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&n.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
             cudaSuccess) {
@@ -72,18 +98,7 @@ const DeviceInfo* current_device_info(int* status) {
 }
 
 uint64_t wait_timeout_ns() { return g_timeout_ns; }
-int debug_flags() {
-  static const int env_flags = static_cast<int>(env_int("TMS_DEBUG_FLAGS", 0));
-  return g_debug_flags | env_flags;
-}
-
-long env_int(const char* name, long fallback) {
-  const char* v = std::getenv(name);
-  if (!v || !*v) return fallback;
-  char* end = nullptr;
-  const long x = std::strtol(v, &end, 10);
-  return (end && *end == '\0') ? x : fallback;
-}
+int debug_flags() { return g_debug_flags; }
 
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,

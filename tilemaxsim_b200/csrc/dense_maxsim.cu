@@ -95,8 +95,7 @@ struct DenseArgs {
   int64_t res_ncent;
   int res_nbits;      // 0: PQ mode; 1, 2 or 4: residual mode
   int res_normalize;
-  int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits);
-                       // bits 2/3: skip the epilogue math / the MMAs (timing experiments only)
+  int debug_flags;     // bit 0: producer issues no load (exercises the bounded waits)
 };
 
 // Shared-memory carve-up, identical on host and device. `split` (one query of <= 32 tokens) adds
@@ -649,7 +648,6 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc(128, TN, a.ab_format);
-      const bool skip_mma = (a.debug_flags & 8) != 0;
       bool ok = true;
       if (QRES && tok_hi > tok_lo) ok = mbar_wait(qfull_bar, 0, abort_flag, tmo, a.err, 3);
       int s = 0;
@@ -681,14 +679,12 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
             // 16-byte units, so each 32-byte K step adds 2
             const uint64_t ad0 = sw128_kmajor_desc(a_base);
             const uint64_t bd0 = sw128_kmajor_desc(b_base);
-            if (!skip_mma) {
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                if (TF32)
-                  mma_tf32(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
-                else
-                  mma_f16(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
-              }
+            for (int k = 0; k < 4; ++k) {
+              if (TF32)
+                mma_tf32(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
+              else
+                mma_f16(d_tmem, ad0 + 2u * k, bd0 + 2u * k, idesc, (c | k) != 0);
             }
             if (!QRES) {
               mma_commit(empty_bar(s));
@@ -746,7 +742,6 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
       if (lane == 0) w = mbar_wait(accf_bar(slot), (uu / NSLOT) & 1u, abort_flag, tmo, a.err, 8);
       return __shfl_sync(0xffffffffu, w, 0) != 0;
     };
-    const bool skip_math = (a.debug_flags & 4) != 0;
 
     int64_t doc = doc_lo;
     int64_t dend = doc_end(doc);
@@ -781,7 +776,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
           uint32_t r[32];
           tmem_ld32_async(t_lane + slot * TN + pc0, r);
           tmem_wait_ld32(r);
-          if (!skip_math) {
+          {
             auto rel = [&](int64_t e) -> int {
               const int64_t x = e - t0;
               return x > 4 * TN ? 4 * TN : static_cast<int>(x);
@@ -838,7 +833,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
             : "memory");
         if (!(ok = all_ok != 0)) break;
         const int n_parts = (ncol + 31) / 32;
-        if (!skip_math) {
+        {
           if (ew == 0) {
             for (int pp = 0; pp < n_parts; ++pp) {
               running = fmaxf(running, xhead[pp * 32 + lane]);
@@ -852,7 +847,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
           dend = xmeta[n_parts - 1].end_dend;
         }
       }
-      if (ok && ew == 0 && !skip_math) {
+      if (ok && ew == 0) {
         for (int64_t dd = doc; dd < doc_hi; ++dd) {
           emit(0, dd, running);
           running = kNegInf;
@@ -889,7 +884,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
         float head = kNegInf, tail = kNegInf;
         int has_b = 0;
         int64_t head_doc = -1, dd = doc, de = dend;
-        if (w_ok && chunk_ok && pw < W && pc0 < ncol && !skip_math) {
+        if (w_ok && chunk_ok && pw < W && pc0 < ncol) {
           auto rel = [&](int64_t e) -> int {
             const int64_t x = e - t0;
             return x > 4 * TN ? 4 * TN : static_cast<int>(x);
@@ -993,7 +988,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
             : "memory");
         if (!(ok = all_ok != 0)) break;
         const int n_parts = (ncol + PC - 1) / PC;
-        if (!skip_math) {
+        {
           if (pw == 0 && chunk_ok) {
             for (int pp = 0; pp < n_parts; ++pp) {
               const int xe = nc * pp + ((c - 2) & (nc - 1));  // the warp owning part pp of chunk c
@@ -1010,7 +1005,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
           dend = xmeta[xl].end_dend;
         }
       }
-      if (ok && pw == 0 && chunk_ok && !skip_math) {
+      if (ok && pw == 0 && chunk_ok) {
         for (int64_t dd = doc; dd < doc_hi; ++dd) {
           emit(c, dd, running);
           running = kNegInf;
@@ -1029,7 +1024,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
           tc_fence_after();
           const int chunk = (m_first + m) * 4 + lg;
           bool released = false;
-          if (chunk < a.n_chunks_total && !skip_math) {
+          if (chunk < a.n_chunks_total) {
             float rm = carry[m * kQTileRows + row];
             int64_t dd = doc, de = dend;
             // Columns of this tile: [0, ncol) are tokens of the range; the open document ends
@@ -1116,7 +1111,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
         doc = next_doc;
         dend = next_dend;
       }
-      if (ok && !skip_math) {
+      if (ok) {
         // Documents still open at the end of the range: the last one (ends at tok_hi) and any
         // empty documents after it.
         for (int m = 0; m < g_this; ++m) {
@@ -1219,16 +1214,15 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   // whole port), and for d > 128 the TMA writes of the streamed chunks share the same port
   // (measured at 16 queries x 50k x 256 tokens: d=768 9.7 ms vs 12.2 ms with 128-token tiles,
   // d=256 3.1 vs 3.3 ms). The cost is two TMEM accumulator slots instead of four.
-  p->TN = static_cast<int>(env_int("TMS_DENSE_TN", prefer_tn ? prefer_tn : 256));
+  p->TN = prefer_tn ? prefer_tn : 256;
   if (p->TN != 128 && p->TN != 256) p->TN = 256;
   const int stage_d = p->kc * p->TN * 128;
   const int qtile = p->kc * static_cast<int>(kQChunkBytes);
-  const bool force_stream = env_int("TMS_DENSE_STREAM", 0) != 0;
-  p->qres = !force_stream && (qtile + 2 * stage_d <= budget);
+  p->qres = qtile + 2 * stage_d <= budget;
   if (cb_bytes && !p->qres) return TMS_ERR_UNSUPPORTED;  // the PQ variant keeps Q resident
   if (p->qres) {
     int gmax = (budget - 2 * stage_d) / qtile;
-    gmax = static_cast<int>(env_int("TMS_DENSE_G", gmax < 4 ? gmax : 4));
+    gmax = gmax < 4 ? gmax : 4;
     if (gmax < 1) gmax = 1;
     // Per-CTA time grows with G x ceil(n_mtiles / G) (units per tile x token share), and an odd
     // G (> 0) runs the epilogue on one warp group instead of two: take the group size that
@@ -1243,22 +1237,21 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
     p->G = (p->n_mtiles + p->n_groups - 1) / p->n_groups;
     int st = (budget - p->G * qtile) / stage_d;
     st = st > 4 ? 4 : st;
-    p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
+    p->stages = st;
   } else {
     const int stage = static_cast<int>(kQChunkBytes) + p->TN * 128;
     int g = p->n_mtiles < 4 ? p->n_mtiles : 4;
-    g = static_cast<int>(env_int("TMS_DENSE_G", g));
     p->n_groups = (p->n_mtiles + g - 1) / g;
     p->G = (p->n_mtiles + p->n_groups - 1) / p->n_groups;
     int st = budget / stage;
     st = st > 6 ? 6 : st;
-    p->stages = static_cast<int>(env_int("TMS_DENSE_STAGES", st));
+    p->stages = st;
   }
   if (p->stages < 1) p->stages = 1;
   const bool split = p->n_mtiles == 1;
   // the estimate above reserved a fixed allowance for barriers / carries / exchange area: move
   // the stage count to what the exact layout allows (at most 4)
-  if (env_int("TMS_DENSE_STAGES", 0) == 0) {
+  {
     while (p->stages > 1 && static_cast<int>(dense_smem_layout(p->TN, p->qres, p->G, p->kc, p->stages,
                                                                split, p->cb_bytes).total) > max_smem)
       --p->stages;
@@ -1274,7 +1267,6 @@ int plan_dense(int dtype, int64_t n_queries, int64_t nq, int64_t d, int64_t n_do
   while (gb) { const int64_t t = gcd % gb; gcd = gb; gb = t; }
   int64_t ranges = num_sms / gcd;
   if (p->n_groups < num_sms && ranges < num_sms / p->n_groups) ranges = num_sms / p->n_groups;
-  ranges = env_int("TMS_DENSE_RANGES", ranges);
   const int64_t tiles = (n_tokens + p->TN - 1) / p->TN;
   if (ranges > tiles) ranges = tiles;
   if (ranges > n_docs) ranges = n_docs;
@@ -1580,22 +1572,30 @@ constexpr size_t kNoAllocAlign = 1024;                     // the workspace alig
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes + kNoAllocAlign];
 
 std::mutex g_noalloc_mutex;
-uint8_t* g_noalloc_base[64] = {};  // device address of the array, per device, 1024-aligned
+struct NoAllocBase {
+  void* ctx;      // context the address was looked up in
+  uint8_t* base;  // device address of the array, 1024-aligned
+};
+NoAllocBase g_noalloc_base[64] = {};
 
-// Host code must not use the array's name as a device address: look the address up once per
-// device, with that device current, and cache it.
+// Host code must not use the array's name as a device address: look the address up with the
+// device current and cache it per device and context (a new context, e.g. after cudaDeviceReset,
+// loads the module again at another address, so the lookup is repeated there).
 int noalloc_scratch(uint8_t** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TMS_ERR_CUDA;
+  void* ctx = current_cu_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_base[dev]) {
+  NoAllocBase& b = g_noalloc_base[dev];
+  if (!b.base || b.ctx != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) return TMS_ERR_CUDA;
     const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + kNoAllocAlign - 1) & ~(kNoAllocAlign - 1);
-    g_noalloc_base[dev] = reinterpret_cast<uint8_t*>(a);
+    b.base = reinterpret_cast<uint8_t*>(a);
+    b.ctx = current_cu_context();  // cudaGetSymbolAddress may have made the primary context current
   }
-  *out = g_noalloc_base[dev];
+  *out = b.base;
   return TMS_OK;
 }
 
@@ -1609,13 +1609,17 @@ extern "C" int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_quer
   NvtxRange nvtx_range("tms_dense_maxsim_noalloc");
   // Nothing in the scratch has to start at zero: the pack kernel writes every byte of the query
   // tiles (padding included) and every partial sum is written before it is read.
+  // The scratch size depends only on the problem (packed query tiles and per-chunk partial sums),
+  // not on the device: tms_dense_workspace_size plans with fixed device facts, and the check
+  // below on the inner call's answer covers any future dependence on the real device.
   const size_t need = tms_dense_workspace_size(dtype, n_queries, nq, d, n_docs, out_mode);
   if (need > kNoAllocScratchBytes) return TMS_ERR_TOO_LARGE;
   uint8_t* scratch = nullptr;
-  const int rc = noalloc_scratch(&scratch);
+  int rc = noalloc_scratch(&scratch);
   if (rc != TMS_OK) return rc;
-  return tms_dense_maxsim(Q, dtype, n_queries, nq, d, D, n_tokens, doc_offsets, n_docs, nd_uniform,
-                          out, out_mode, scratch, kNoAllocScratchBytes, stream);
+  rc = tms_dense_maxsim(Q, dtype, n_queries, nq, d, D, n_tokens, doc_offsets, n_docs, nd_uniform,
+                        out, out_mode, scratch, kNoAllocScratchBytes, stream);
+  return rc == TMS_ERR_WORKSPACE ? TMS_ERR_TOO_LARGE : rc;
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -442,7 +442,7 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   // as many slots as TMEM holds: a hand-off through an mbarrier takes ~500 cycles, so several
   // tiles must be in flight between the decoders, the MMA and the epilogue
   int nslot = 512 / (acols + N);
-  nslot = static_cast<int>(env_int("TMS_PQ_NSLOT", nslot > 8 ? 8 : nslot));
+  if (nslot > 8) nslot = 8;
   if (nslot < 2 || nslot * (acols + N) > 512) return TMS_ERR_UNSUPPORTED;
   const size_t need = pq_tokrows_workspace_size(n_queries, nq, n_docs);
   if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
@@ -468,7 +468,7 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   a.nslot = nslot;
   a.debug_flags = debug_flags();
   // one CTA per SM (a persistent range each), fewer for small corpora
-  int64_t ranges = env_int("TMS_PQ_RANGES", dev->num_sms);
+  int64_t ranges = dev->num_sms;
   const int64_t min_tiles = (n_tokens + 127) / 128;
   if (ranges > min_tiles) ranges = min_tiles;
   if (ranges > n_docs) ranges = n_docs;

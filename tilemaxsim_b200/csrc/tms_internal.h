@@ -15,12 +15,16 @@ namespace tms {
 // Per-device facts and the address of the device error word (set up once per device).
 struct DeviceInfo {
   int device = -1;
+  void* ctx = nullptr;  // the CUcontext current when the entry was filled in
   int num_sms = 0;
   int max_smem_optin = 0;
   uint32_t* err_word = nullptr;
 };
 // Returns nullptr (and sets *status) when the current device cannot be queried.
 const DeviceInfo* current_device_info(int* status);
+// The calling thread's current CUcontext (nullptr when none): addresses of __device__ variables
+// are only valid in the context they were looked up in.
+void* current_cu_context();
 
 // Wait limit for the bounded mbarrier waits, in nanoseconds (default 2 s; tms_set_debug changes it).
 uint64_t wait_timeout_ns();
@@ -32,9 +36,6 @@ int debug_flags();
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_rows);
-
-// Integer environment override (tuning and benchmarking only); `fallback` when unset.
-long env_int(const char* name, long fallback);
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TMS_OK : TMS_ERR_CUDA; }
 

@@ -3,9 +3,10 @@
 Each rank holds a contiguous shard of the corpus (its documents' tokens + int64 offsets) and the
 global id of its first document. A search scores every query against the local shard (one
 tcgen05 launch), keeps the local top-k with global ids, and merges the shards' lists with ONE
-all-gather (NCCL over NVLink/NVSwitch in production, gloo in the CPU tests) followed by a top-k of
-the world*k candidates under the same rule: score descending, then global id ascending. The
-result is identical on every rank and equal to a single-GPU top-k over the whole corpus.
+all-gather of a packed (ids, score bits) buffer (NCCL over NVLink/NVSwitch in production, gloo in
+the CPU tests) followed by a top-k of the world*k candidates under the same rule: score
+descending, then global id ascending. The result is identical on every rank and equal to a
+single-GPU top-k over the whole corpus.
 
 The reference has no distributed path (its "multi-GPU" experiment ran independent halves from one
 process with no merge, src/run_all_experiments.py:355-443); this is additive API.
@@ -46,12 +47,15 @@ def merge_topk(vals: torch.Tensor, ids: torch.Tensor, k: int, group=None,
         return vals, ids
     world = dist.get_world_size(group)
     rows = vals.shape[0]
-    gv = torch.empty((world * rows, k), dtype=vals.dtype, device=vals.device)
-    gi = torch.empty((world * rows, k), dtype=ids.dtype, device=ids.device)
-    dist.all_gather_into_tensor(gv, vals, group=group)  # rank-major concatenation along dim 0
-    dist.all_gather_into_tensor(gi, ids, group=group)
-    cand_v = gv.view(world, rows, k).permute(1, 0, 2).reshape(rows, world * k)
-    cand_i = gi.view(world, rows, k).permute(1, 0, 2).reshape(rows, world * k)
+    # one collective: ids and the scores' bit patterns travel in one int64 buffer (rows, 2k)
+    packed = torch.empty((rows, 2 * k), dtype=torch.int64, device=vals.device)
+    packed[:, :k] = ids
+    packed[:, k:] = vals.view(torch.int32).to(torch.int64)
+    gathered = torch.empty((world * rows, 2 * k), dtype=torch.int64, device=vals.device)
+    dist.all_gather_into_tensor(gathered, packed, group=group)  # rank-major along dim 0
+    g = gathered.view(world, rows, 2 * k).permute(1, 0, 2)  # (rows, world, 2k)
+    cand_i = g[:, :, :k].reshape(rows, world * k)
+    cand_v = g[:, :, k:].reshape(rows, world * k).to(torch.int32).view(torch.float32)
     fn = topk_fn or topk
     return fn(cand_v.contiguous(), k, ids=cand_i.contiguous())
 
