@@ -172,6 +172,43 @@ __device__ __forceinline__ float range_max32(float acc, const uint32_t (&r)[32],
   return fmaxf(m0, m1);
 }
 
+// max(init, r[LO..HI)) over compile-time column ranges, two independent chains.
+template <int LO, int HI>
+__device__ __forceinline__ float cmax(float init, const uint32_t (&r)[32]) {
+  float m0 = init, m1 = kNegInf;
+#pragma unroll
+  for (int i = LO; i < HI; i += 4) {
+    if (i + 1 < HI) m0 = fmax3(m0, u2f(r[i]), u2f(r[i + 1]));
+    else m0 = fmaxf(m0, u2f(r[i]));
+    if (i + 3 < HI) m1 = fmax3(m1, u2f(r[i + 2]), u2f(r[i + 3]));
+    else if (i + 2 < HI) m1 = fmaxf(m1, u2f(r[i + 2]));
+  }
+  return fmaxf(m0, m1);
+}
+
+// A 32-column block with one document boundary at column p (warp-uniform, 0 <= p < 32):
+// acc = max(acc, r[0..p)) and the return value is max(r[p..32)). A jump over 32 straight-line
+// variants costs one indirect branch instead of a select per column.
+template <int P>
+__device__ __forceinline__ float split_at(float& acc, const uint32_t (&r)[32]) {
+  acc = cmax<0, P>(acc, r);
+  return cmax<P, 32>(kNegInf, r);
+}
+__device__ __forceinline__ float split_max32(float& acc, const uint32_t (&r)[32], int p) {
+  switch (p) {
+#define TMS_SPLIT_CASE(n) case n: return split_at<n>(acc, r);
+    TMS_SPLIT_CASE(0) TMS_SPLIT_CASE(1) TMS_SPLIT_CASE(2) TMS_SPLIT_CASE(3) TMS_SPLIT_CASE(4)
+    TMS_SPLIT_CASE(5) TMS_SPLIT_CASE(6) TMS_SPLIT_CASE(7) TMS_SPLIT_CASE(8) TMS_SPLIT_CASE(9)
+    TMS_SPLIT_CASE(10) TMS_SPLIT_CASE(11) TMS_SPLIT_CASE(12) TMS_SPLIT_CASE(13) TMS_SPLIT_CASE(14)
+    TMS_SPLIT_CASE(15) TMS_SPLIT_CASE(16) TMS_SPLIT_CASE(17) TMS_SPLIT_CASE(18) TMS_SPLIT_CASE(19)
+    TMS_SPLIT_CASE(20) TMS_SPLIT_CASE(21) TMS_SPLIT_CASE(22) TMS_SPLIT_CASE(23) TMS_SPLIT_CASE(24)
+    TMS_SPLIT_CASE(25) TMS_SPLIT_CASE(26) TMS_SPLIT_CASE(27) TMS_SPLIT_CASE(28) TMS_SPLIT_CASE(29)
+    TMS_SPLIT_CASE(30)
+#undef TMS_SPLIT_CASE
+    default: return split_at<31>(acc, r);
+  }
+}
+
 // Residual decoding works from a two-slot ring of shared memory that the decoder warps fill one
 // tile ahead with asynchronous copies, so the L2 gathers of centroid rows overlap the decoding of
 // the previous tile instead of stalling it. Before the ring, a byte table: for each byte value,
@@ -1040,7 +1077,23 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
             auto reduce32 = [&](const uint32_t(&v)[32], int cb) {
               if (dcol >= cb + 32 && ncol >= cb + 32) {
                 rm = max32(rm, v);  // the whole block lies in the open document
-              } else {
+                return;
+              }
+              if (ncol >= cb + 32) {
+                // a full block whose only boundary is the open document's end
+                const int64_t de2 = doc_end(dd + 1);
+                const int dcol2 = rel(de2);
+                if (dcol2 >= cb + 32) {
+                  const float next = split_max32(rm, v, dcol - cb);
+                  emit(chunk, dd, rm);
+                  rm = next;
+                  ++dd;
+                  de = de2;
+                  dcol = dcol2;
+                  return;
+                }
+              }
+              {
                 const int n = (ncol - cb < 32) ? ncol - cb : 32;
                 int lo = 0;
                 while (true) {
