@@ -157,30 +157,33 @@ __global__ void __launch_bounds__(kPqThreads)
   }
 }
 
-// Bank-conflict-free table lookups (M % 4 == 0, the common shapes M = 8 and 16).
+// Bank-conflict-free table lookups (M = 8 or 16).
 //
 // The kernel above gives each lane its own document token, so the 32 lanes of a load read table
 // rows chosen by 32 random codes and collide in the shared-memory banks (about 2.4 wavefronts per
-// ideal one at M = 16). Here the lanes of a warp work on the SAME token: lane = (g, i) with
+// ideal one at M = 16). Here the lanes of a warp work on the SAME four tokens: lane = (g, i) with
 // i = lane & 7 the query token of the slice and g = lane >> 3 one of four subspace groups
-// (subspaces m = 4a + g, a = 0 .. M/4-1). The table is stored as rows of 32 floats,
+// (subspaces m = A g + aa, aa = 0 .. A-1, A = M / 4: the group's A consecutive code bytes). The
+// table is stored as rows of 32 floats,
 //
-//     T4[a][k][8 g + i] = <Q[q, i0 + i, m-slice], C[m, k]>,   m = 4a + g,
+//     T4[aa][k][8 g + i] = <Q[q, i0 + i, m-slice], C[m, k]>,   m = A g + aa,
 //
-// so at every step a the four lane groups read four rows picked by four different codes, but each
-// group only ever touches its own eight banks (8 g .. 8 g + 7): every load is one wavefront,
-// whatever the codes are. Each lane sums its M/4 subspaces; four tokens are processed together and
-// a two-round reduce-scatter over the lane groups (3 shuffles) leaves the full sum of token g in
-// lane group g, which keeps a running max over its tokens of the document. At the document's end
-// the groups' maxima are merged (2 shuffles) and the 8 query tokens summed (3 shuffles).
-// Per 4 tokens and 8 query tokens: 4 uniform 16-byte code loads, 4 M/4 table loads and 3 shuffles.
-// The m-summation order is (groups of 4 subspaces, then across groups) instead of the reference's
-// m = 0, 1, 2, ...: the sums differ only by fp32 rounding.
+// (rows of code bytes aa = 2 rp and 2 rp + 1 interleaved in 256-byte row pairs, so that one byte
+// permute turns a code byte into the entry's offset),
+// so at every step aa the four lane groups read four rows picked by four different codes, but
+// each group only ever touches its own eight banks (8 g .. 8 g + 7): every load is one wavefront,
+// whatever the codes are. A lane group loads only its own A code bytes of a token (one 4- or
+// 2-byte load; the warp's four groups read four tokens inside one 64-byte span), sums its A
+// subspaces, and a two-round reduce-scatter over the lane groups (3 shuffles per four tokens)
+// leaves the full sum of token j0 + g in lane group g, which keeps a running max over its tokens
+// of the document. At the document's end the groups' maxima are merged (2 shuffles) and the 8
+// query tokens summed (3 shuffles). The m-summation order is (groups of A subspaces, then across
+// groups) instead of the reference's m = 0, 1, 2, ...: the sums differ only by fp32 rounding.
 constexpr int kLut4Threads = 512;
 
 template <int A, int KT>  // A = M / 4 table rows per token; KT = K when it is 256, else 0
 __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a) {
-  extern __shared__ __align__(128) float tbl4[];  // [A][K][32]
+  extern __shared__ __align__(128) float tbl4[];  // [A / 2][K][2][32]
   const int n_slices = gridDim.x / a.n_doc_parts;
   // consecutive CTAs share a document range (and its codes in L2) and differ in query slice
   const int slice_id = blockIdx.x % n_slices;
@@ -190,11 +193,14 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
   const int d = a.M * a.dsub;
   const int K = KT ? KT : a.K;
 
+  // entry e = ((rp * K + k) * 2 + half) * 32 + col holds subspace byte aa = 2 rp + half
   for (int e = threadIdx.x; e < A * K * 32; e += blockDim.x) {
     const int col = e & 31;
-    const int ak = e >> 5;
-    const int aa = ak / K, k = ak - aa * K;
-    const int m = 4 * aa + (col >> 3);
+    const int half = (e >> 5) & 1;
+    const int rk = e >> 6;
+    const int rp = rk / K, k = rk - rp * K;
+    const int aa = 2 * rp + half;
+    const int m = A * (col >> 3) + aa;
     const int i = i0 + (col & 7);
     float acc = 0.0f;
     if (i < a.nq) {
@@ -215,56 +221,53 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
   const int64_t doc_end = n_docs * (part + 1) / a.n_doc_parts;
   const int ns = min(8, a.nq - i0);
   const uint32_t kmax = static_cast<uint32_t>(K - 1);
-  // Byte g of a code word, scaled to the 128-byte table row and or-ed with this lane's column:
-  // a funnel rotate brings bits [8g, 8g + 8) to [7, 15), one 3-input logic op masks them and
-  // inserts lane * 4 (bits 0-6, zero after the mask).
-  const uint32_t rot = static_cast<uint32_t>(8 * g - 7) & 31u;
+  // Byte offset of this lane's entry for code byte aa inside its 256-byte row pair: code * 256
+  // + lane * 4, built by one byte permute (byte 1 = the code, byte 0 = lane * 4 < 128, bytes 2-3
+  // = zero bytes of lane4); the row pair and half go into the load's immediate offset.
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
-  auto row_off = [&](uint32_t w) -> uint32_t {
+  auto row_off = [&](uint32_t w, int aa) -> uint32_t {
     if constexpr (KT == 256) {
-      return (__funnelshift_r(w, w, rot) & 0x7f80u) | lane4;
+      return __byte_perm(w, lane4, 0x5504u | (static_cast<uint32_t>(aa) << 4));
     } else {
-      const uint32_t code = min((w >> (8 * g)) & 0xffu, kmax);  // a code >= K never reads past the table
-      return (code << 7) | lane4;
+      const uint32_t code = min((w >> (8 * aa)) & 0xffu, kmax);  // a code >= K never reads past the table
+      return (code << 8) | lane4;
     }
   };
   const char* tb = reinterpret_cast<const char*>(tbl4);
   auto lookup = [&](int aa, uint32_t off) -> float {
-    return *reinterpret_cast<const float*>(tb + static_cast<uint32_t>(aa * K * 128) + off);
+    return *reinterpret_cast<const float*>(tb + static_cast<uint32_t>((aa >> 1) * K * 256 + (aa & 1) * 128) + off);
   };
-  using CodeVec = typename std::conditional<A == 4, uint4, uint2>::type;
-  auto word = [](const CodeVec& c, int aa) -> uint32_t {
-    if constexpr (A == 4) return aa == 0 ? c.x : aa == 1 ? c.y : aa == 2 ? c.z : c.w;
-    else return aa == 0 ? c.x : c.y;
-  };
+  // lane group g reads only its own A code bytes of a token: one 4-byte (M = 16) or 2-byte
+  // (M = 8) load, four different tokens per warp instruction inside one 64-byte span
+  using CodeWord = typename std::conditional<A == 4, uint32_t, uint16_t>::type;
 
   for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
     // clamped to the code rows that exist, so malformed offsets never read outside `codes`
     const int64_t t_lo = max(min(a.docs.start(doc), a.n_tokens), int64_t(0));
     const int64_t t_hi = max(min(a.docs.start(doc + 1), a.n_tokens), t_lo);
     const int len = static_cast<int>(min(t_hi - t_lo, int64_t(0x7fffffff)));
-    const CodeVec* rows = reinterpret_cast<const CodeVec*>(a.codes) + t_lo;
+    const CodeWord* words = reinterpret_cast<const CodeWord*>(a.codes + t_lo * (4 * A)) + g;
     float run = kNegInfPq;
     // Lane group g handles the four tokens of a step in the order j0 + (t ^ g): after the
     // reduce-scatter below its own token j0 + g then needs no select.
-    auto load4 = [&](int j0, CodeVec (&c)[4]) {
+    auto load4 = [&](int j0, uint32_t (&c)[4]) {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) c[t] = __ldg(rows + min(j0 + (t ^ g), len - 1));
+      for (int t = 0; t < 4; ++t) c[t] = __ldg(words + 4 * min(j0 + (t ^ g), len - 1));
     };
     if (len > 0) {
-      CodeVec nxt[4];
+      uint32_t nxt[4];
       load4(0, nxt);
       for (int j0 = 0; j0 < len; j0 += 4) {
-        CodeVec cur[4];
+        uint32_t cur[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) cur[t] = nxt[t];
         load4(j0 + 4, nxt);  // the next four tokens' codes in flight
         float p[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          float acc = lookup(0, row_off(word(cur[t], 0)));
+          float acc = lookup(0, row_off(cur[t], 0));
 #pragma unroll
-          for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(word(cur[t], aa)));
+          for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(cur[t], aa));
           p[t] = acc;  // token j0 + (t ^ g), this lane's subspaces
         }
         // reduce-scatter over the lane groups: the partner g ^ 2 holds tokens j0 + g (its t = 2)
