@@ -736,6 +736,8 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device, emit: bool 
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if world == 1 and args.config == "c5":
+        out["bounded_memory_topk"] = chunked_topk_times(Qd, D, off, k, n_docs)
     if emit and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg)
     if emit and world == 1 and args.config == "c2" and not args.no_legs:
@@ -743,6 +745,28 @@ def run_ours(args, cfg, rank: int, world: int, device: torch.device, emit: bool 
     if emit:
         emit_json(out)
     return out
+
+
+def chunked_topk_times(Q, D, off, k: int, n_docs: int, reps: int = 3) -> dict:
+    """The bounded-memory search (tms_dense_maxsim_topk: documents scored a chunk at a time into
+    one reused buffer, each chunk's top-k merged into a running list) against the full-matrix
+    path timed above (whole (B_q, n) score matrix, then one top-k): device time per search and
+    the score buffer each holds."""
+    import tilemaxsim_b200 as tms
+    res = {}
+    for chunk in (n_docs // 10, n_docs // 2):
+        tms.maxsim_topk(Q, D, off, k, chunk_docs=chunk)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            tms.maxsim_topk(Q, D, off, k, chunk_docs=chunk)
+        e1.record()
+        torch.cuda.synchronize()
+        res[f"chunk_docs={chunk}"] = {"ms": e0.elapsed_time(e1) / reps,
+                                      "score_buffer_mb": Q.shape[0] * chunk * 4 / 2**20}
+    res["full_matrix_score_buffer_mb"] = Q.shape[0] * n_docs * 4 / 2**20
+    return res
 
 
 LEGS = ("q1_ragged", "c3_768", "c4")

@@ -462,6 +462,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
   float* carry = reinterpret_cast<float*>(smem + L.carry_off);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 4);
+  volatile int* never_flag = reinterpret_cast<volatile int*>(smem + L.misc_off + 8);  // stays 0
   RangeInfo* rinfo = reinterpret_cast<RangeInfo*>(smem + L.misc_off + 16);
 
   const int warp = threadIdx.x >> 5;
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
     if (RES)  // residual ring slots: one cp.async arrival per decoder thread
       for (int b = 0; b < kResRing; ++b) mbar_init(smem_u32(smem + L.cb_off) + 8u * b, RES * 32);
     *abort_flag = (smem_u32(smem) & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
+    *never_flag = 0;
     if (*abort_flag) atomicCAS(a.err, 0u, kDevErrTimeout | 15u);
     fence_mbar_init();
   }
@@ -571,11 +573,17 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
       }
       int s = 0;
       uint32_t ph = 0;
+      uint32_t armed = 0, armed_par = 0;  // per stage: a load was issued, and its phase parity
+      auto arm = [&](int st_i, uint32_t par, uint32_t bytes) {
+        mbar_arrive_expect_tx(full_bar(st_i), bytes);
+        armed |= 1u << st_i;
+        armed_par = (armed_par & ~(1u << st_i)) | (par << st_i);
+      };
       bool ok = !PQ;  // the PQ variant's D stages are filled by the decoder warps
       for (int64_t t0 = tok_lo; ok && t0 < tok_hi; t0 += TN) {
         if (QRES) {
           if (!(ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 1))) break;
-          mbar_arrive_expect_tx(full_bar(s), static_cast<uint32_t>(a.kc * TN * 128));
+          arm(s, ph, static_cast<uint32_t>(a.kc * TN * 128));
           const uint32_t st = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
           for (int c = 0; c < a.kc; ++c)
             tma_load_2d(st + static_cast<uint32_t>(c * TN * 128), &dmap, full_bar(s), c * cw,
@@ -585,7 +593,7 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
           for (int m = 0; ok && m < g_this; ++m) {
             for (int c = 0; c < a.kc; ++c) {
               if (!(ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, tmo, a.err, 2))) break;
-              mbar_arrive_expect_tx(full_bar(s), kQChunkBytes + TN * 128u);
+              arm(s, ph, kQChunkBytes + TN * 128u);
               const uint32_t st = st_s + static_cast<uint32_t>(s) * L.stage_bytes;
               tma_load_2d(st, &qmap, full_bar(s), c * cw, (m_first + m) * kQTileRows, pol_q);
               tma_load_2d(st + kQChunkBytes, &dmap, full_bar(s), c * cw, static_cast<int32_t>(t0),
@@ -594,6 +602,13 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
             }
           }
         }
+      }
+      if (*abort_flag) {
+        // A wait gave up somewhere in the CTA: before the CTA exits, let every copy this thread
+        // issued land in shared memory (each bounded by the wait limit on its own).
+        if (QRES && tok_hi > tok_lo) mbar_wait(qfull_bar, 0, never_flag, tmo, a.err, 11);
+        for (int st_i = 0; st_i < S; ++st_i)
+          if (armed & (1u << st_i)) mbar_wait(full_bar(st_i), (armed_par >> st_i) & 1u, never_flag, tmo, a.err, 12);
       }
     }
   } else if (PQ && RES && warp >= kDecodeWarp0) {
