@@ -1094,8 +1094,10 @@ __global__ void __launch_bounds__(RES ? res_threads(RES) : PQ ? kPqThreadsMma : 
                 rm = max32(rm, v);  // the whole block lies in the open document
                 return;
               }
-              if (ncol >= cb + 32) {
-                // a full block whose only boundary is the open document's end
+              if (QRES && ncol >= cb + 32) {
+                // a full block whose only boundary is the open document's end (Q-resident
+                // kernels only: compiled into the streaming kernel, the jump put the loaded block
+                // in a 976-byte local-memory frame and made d = 256 / 768 scoring 2-5x slower)
                 const int64_t de2 = doc_end(dd + 1);
                 const int dcol2 = rel(de2);
                 if (dcol2 >= cb + 32) {
