@@ -29,6 +29,13 @@ constexpr int kPqThreads = 512;
 constexpr int kPqTableBudget = 200 * 1024;
 constexpr float kNegInfPq = -__builtin_huge_valf();
 
+// Three-input fp32 max (PTX max.f32 with three sources, sm_100a).
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+  return r;
+}
+
 __device__ __forceinline__ float load_elem(const void* p, int dtype, int64_t i) {
   if (dtype == TMS_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
   if (dtype == TMS_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
@@ -248,34 +255,59 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
     const int len = static_cast<int>(min(t_hi - t_lo, int64_t(0x7fffffff)));
     const CodeWord* words = reinterpret_cast<const CodeWord*>(a.codes + t_lo * (4 * A)) + g;
     float run = kNegInfPq;
-    // Lane group g handles the four tokens of a step in the order j0 + (t ^ g): after the
-    // reduce-scatter below its own token j0 + g then needs no select.
-    auto load4 = [&](int j0, uint32_t (&c)[4]) {
+    // Lane group g handles each group of four tokens in the order j0 + (t ^ g): after the
+    // reduce-scatter below its own token j0 + g then needs no select. A step takes eight tokens
+    // (two independent groups of four); the codes of the next step are in flight meanwhile.
+    const int last = len - 1;
+    auto load8 = [&](int j0, uint32_t (&c)[8], bool clamp) {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) c[t] = __ldg(words + 4 * min(j0 + (t ^ g), len - 1));
+      for (int t = 0; t < 8; ++t) {
+        const int j = j0 + (t & 4) + ((t & 3) ^ g);
+        c[t] = __ldg(words + 4 * (clamp ? min(j, last) : j));
+      }
+    };
+    // the full sum of token j0 + g from this lane's partial sums p[t] of tokens j0 + (t ^ g):
+    // the partner g ^ 2 holds j0 + g (its t = 2) and j0 + (1 ^ g) (its t = 3); then g ^ 1 holds
+    // j0 + g as its t = 1
+    auto reduce4 = [&](const float* p) -> float {
+      const float q0 = p[0] + __shfl_xor_sync(0xffffffffu, p[2], 16);
+      const float q1 = p[1] + __shfl_xor_sync(0xffffffffu, p[3], 16);
+      return q0 + __shfl_xor_sync(0xffffffffu, q1, 8);
+    };
+    auto step = [&](const uint32_t (&c)[8], int j0, bool tail) {
+      float p[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        float acc = lookup(0, row_off(c[t], 0));
+#pragma unroll
+        for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(c[t], aa));
+        p[t] = acc;
+      }
+      const float s0 = reduce4(p), s1 = reduce4(p + 4);
+      if (!tail) {
+        run = fmax3(run, s0, s1);
+      } else {
+        if (j0 + g < len) run = fmaxf(run, s0);
+        if (j0 + 4 + g < len) run = fmaxf(run, s1);
+      }
     };
     if (len > 0) {
-      uint32_t nxt[4];
-      load4(0, nxt);
-      for (int j0 = 0; j0 < len; j0 += 4) {
-        uint32_t cur[4];
+      uint32_t nxt[8];
+      load8(0, nxt, true);
+      int j0 = 0;
+      for (; j0 + 16 <= len; j0 += 8) {  // this step and the next are whole: no clamping
+        uint32_t cur[8];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) cur[t] = nxt[t];
-        load4(j0 + 4, nxt);  // the next four tokens' codes in flight
-        float p[4];
+        for (int t = 0; t < 8; ++t) cur[t] = nxt[t];
+        load8(j0 + 8, nxt, false);
+        step(cur, j0, false);
+      }
+      for (; j0 < len; j0 += 8) {
+        uint32_t cur[8];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float acc = lookup(0, row_off(cur[t], 0));
-#pragma unroll
-          for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(cur[t], aa));
-          p[t] = acc;  // token j0 + (t ^ g), this lane's subspaces
-        }
-        // reduce-scatter over the lane groups: the partner g ^ 2 holds tokens j0 + g (its t = 2)
-        // and j0 + (1 ^ g) (its t = 3); then g ^ 1 holds j0 + g as its t = 1
-        const float q0 = p[0] + __shfl_xor_sync(0xffffffffu, p[2], 16);
-        const float q1 = p[1] + __shfl_xor_sync(0xffffffffu, p[3], 16);
-        const float sum = q0 + __shfl_xor_sync(0xffffffffu, q1, 8);
-        if (j0 + g < len) run = fmaxf(run, sum);
+        for (int t = 0; t < 8; ++t) cur[t] = nxt[t];
+        load8(j0 + 8, nxt, true);
+        step(cur, j0, j0 + 8 > len);
       }
     }
     run = fmaxf(run, __shfl_xor_sync(0xffffffffu, run, 8));
