@@ -193,6 +193,40 @@ TMS_API int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld, i
              const int64_t* ids_in, int64_t ld_ids, int64_t id_base, float* out_vals,
              int64_t* out_ids, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- candidate generation (IVF probe) */
+/* No reference function: the reference reaches a candidate stage only through external searchers
+ * (PLAID's dense_search, src/plaid_integration_benchmark.py:186-211; WARP, baselines/bench_warp.py).
+ * Python: tilemaxsim_b200.IVFIndex. */
+
+/* probe: (n_queries, n_probe) centroid ids (each query's tokens' nprobe best centroids, any order,
+ * ids outside [0, n_centroids) ignored); ivf_offsets (n_centroids + 1) / ivf_docs: inverted lists
+ * (the documents holding a token of each centroid; ids outside [0, n_docs) ignored). Writes
+ * bitmaps ((n_queries + 1) rows of ceil(n_docs / 32) words; row q = query q's candidates, row
+ * n_queries = their union), the union's documents in increasing order into cand_ids (at most
+ * cand_capacity of them) and their number into *cand_count (device). */
+TMS_API int tms_ivf_candidates(const int64_t* probe, int64_t n_queries, int64_t n_probe,
+                               const int64_t* ivf_offsets, const int32_t* ivf_docs,
+                               int64_t n_centroids, int64_t n_docs, uint32_t* bitmaps,
+                               int64_t* cand_ids, int64_t cand_capacity, int64_t* cand_count,
+                               void* stream);
+
+/* out_offsets (n_ids + 1): running token counts of the documents ids[0..n_ids) of a ragged corpus
+ * (ids outside [0, n_docs) count 0 tokens). */
+TMS_API int tms_gather_offsets(const int64_t* doc_offsets, int64_t n_docs, const int64_t* ids,
+                               int64_t n_ids, int64_t* out_offsets, void* stream);
+
+/* Copies the token rows (row_bytes each, a multiple of 16; 16-byte aligned buffers) of documents
+ * ids[0..n_ids) into out, document i at rows [out_offsets[i], out_offsets[i+1]). */
+TMS_API int tms_gather_docs(const void* D, int64_t row_bytes, const int64_t* doc_offsets,
+                            int64_t n_docs, int64_t n_tokens, const int64_t* ids, int64_t n_ids,
+                            const int64_t* out_offsets, int64_t out_tokens, void* out, void* stream);
+
+/* scores (n_queries, n_cand) with row stride ld: entries whose document ids[c] is not set in row
+ * q of bitmaps (as written by tms_ivf_candidates) become `fill`. */
+TMS_API int tms_mask_candidates(float* scores, int64_t n_queries, int64_t n_cand, int64_t ld,
+                                const int64_t* ids, const uint32_t* bitmaps, int64_t n_docs,
+                                float fill, void* stream);
+
 /* ---------------------------------------------------------------- introspection and test hooks */
 
 /* Launch plan the dense kernel would use (no reference counterpart): info[0..9] = tokens per tile,

@@ -165,3 +165,13 @@ def test_residual_layout_matches_colbert_encoder(nbits):
     unit = O.residual_decompress(C.astype(np.float16), codes, packed, w, nbits, normalize=True).astype(np.float32)
     cos = (unit * X).sum(axis=1)
     assert cos.min() > 0.9
+
+
+def test_ivf_oracle_lists_and_candidates():
+    """The IVF restatement on a hand-made corpus: three documents over four centroids."""
+    codes = np.array([0, 2, 2, 1, 3, 0, 9], dtype=np.int32)  # 9 is outside the table
+    off = np.array([0, 3, 5, 7])  # doc0: {0, 2}, doc1: {1, 3}, doc2: {0}
+    lists = O.ivf_lists(codes, off, 4)
+    assert [list(x) for x in lists] == [[0, 2], [1], [0], [1]]
+    cands = O.ivf_candidates(np.array([[2, 3], [1, 1], [7, 0]]), lists)
+    assert [list(c) for c in cands] == [[0, 1], [1], [0, 2]]

@@ -38,6 +38,10 @@ SIGNATURES = {
     "tms_set_debug": (None, [_u64, _i32]),
     "tms_validate_offsets": (_i32, [_vp, _i64, _i64, _vp]),
     "tms_dense_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i32]),
+    "tms_ivf_candidates": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "tms_gather_offsets": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp]),
+    "tms_gather_docs": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),
+    "tms_mask_candidates": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, ctypes.c_float, _vp]),
     "tms_dense_maxsim": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _i32,
                                 _vp, _sz, _vp]),
     "tms_dense_maxsim_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp,
