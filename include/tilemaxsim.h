@@ -53,7 +53,11 @@ extern "C" {
 
 /* PQ modes */
 #define TMS_PQ_FAST 0  /* tensor cores where the shape allows (fp16 codebook) */
-#define TMS_PQ_EXACT 1 /* fp32 table lookups, the reference precision (Python default) */
+#define TMS_PQ_EXACT 1 /* fp32 table lookups, the reference precision */
+#define TMS_PQ_PRECISE 2 /* the reference precision, by the fastest kernel that keeps it (Python
+                            default): fp16 queries of 1-2 chunks of 32 rows on the tensor cores
+                            with the codebook split into fp16 hi + lo (|codebook| < 65504, the
+                            caller's guarantee), everything else by the fp32 table lookups */
 
 /* dense output modes */
 #define TMS_OUT_SCORE 0     /* out[q * n_docs + doc] = sum_i max_j <Q_qi, D_j>                 */

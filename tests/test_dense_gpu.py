@@ -169,7 +169,7 @@ def test_full_size_rerank_consistency(cuda_device):
     close(sub, O.maxsim_ragged(Qb.cpu(), Dsub.cpu(), sub_off))
 
 
-@pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor", "pq_token_rows"])
+@pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor", "pq_token_rows", "pq_precise"])
 def test_bounded_wait_reports_timeout(case, cuda_device):
     """Fault knob: the producer issues no load, so every consumer wait runs out after the (short)
     limit; the kernel returns, the host reads TMS_ERR_TIMEOUT, and the context stays usable."""
@@ -177,7 +177,7 @@ def test_bounded_wait_reports_timeout(case, cuda_device):
     lib = _lib.load()
     if case.startswith("pq"):
         cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
-        pq = TileMaxSimPQ(cb, exact=False)
+        pq = TileMaxSimPQ(cb, exact=(case == "pq_precise"))
         codes = torch.randint(0, 256, (40 * 64, 16), generator=R.gen(4), dtype=torch.uint8).to(cuda_device)
         off = (torch.arange(41, dtype=torch.int64) * 64).to(cuda_device)
         # 5 queries: decoder-warp variant of the dense kernel; 1 query: token-rows kernel

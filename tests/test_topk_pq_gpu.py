@@ -238,3 +238,28 @@ def test_pq_exact_c4_full_size_document_independence(cuda_device):
     assert torch.equal(full[:, pick], sub)
     want = O.pq_maxsim_adc_ragged(Qb.cpu(), cb.cpu(), sub_codes.cpu(), sub_off.cpu().numpy())
     np.testing.assert_allclose(sub.cpu().numpy(), want, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("nqry,nq,lengths", [(1, 32, "c4"), (2, 32, "c4"), (1, 64, "ragged"),
+                                              (2, 20, "ragged"), (1, 5, "tiny")])
+def test_pq_precise_tensor_path_vs_oracle(nqry, nq, lengths, cuda_device):
+    """One or two fp16 queries at the default precision run on the tensor cores with the codebook
+    split into fp16 hi + lo: scores within 1e-5 relative of the reference's fp32 ADC arithmetic."""
+    from tilemaxsim_b200 import TileMaxSimPQ, _lib
+    if lengths == "c4":
+        off = np.arange(2001, dtype=np.int64) * 128
+    elif lengths == "ragged":
+        off = R.offsets_from_lengths(R.ragged_lengths(900, 0, 300, seed=nq))
+    else:
+        off = R.offsets_from_lengths(R.ragged_lengths(3000, 0, 3, seed=7))
+    cb = R.randn((16, 256, 8), 3, torch.float32)
+    Qb = R.normalized((nqry, nq, 128), 4)
+    codes = torch.randint(0, 256, (int(off[-1]), 16), generator=R.gen(5), dtype=torch.uint8)
+    pq = TileMaxSimPQ(cb.to(cuda_device))
+    assert pq._mode() == _lib.TMS_PQ_PRECISE
+    got = pq.score_queries(Qb.to(cuda_device), codes.to(cuda_device),
+                           torch.from_numpy(off).to(cuda_device)).cpu().numpy()
+    want = O.pq_maxsim_adc_ragged(Qb, cb, codes, off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-5, atol=1e-4)

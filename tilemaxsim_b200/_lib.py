@@ -25,7 +25,7 @@ TMS_ERR_BAD_OFFSETS = 7
 
 TMS_F16, TMS_BF16, TMS_F32 = 0, 1, 2
 TMS_OUT_SCORE, TMS_OUT_TOKEN_MAX = 0, 1
-TMS_PQ_FAST, TMS_PQ_EXACT = 0, 1
+TMS_PQ_FAST, TMS_PQ_EXACT, TMS_PQ_PRECISE = 0, 1, 2
 
 DTYPE_CODE = {torch.float16: TMS_F16, torch.bfloat16: TMS_BF16, torch.float32: TMS_F32}
 

@@ -407,7 +407,7 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
                              float* out, int mode, void* workspace, size_t workspace_bytes,
                              void* stream) {
   NvtxRange nvtx_range("tms_pq_maxsim");
-  if (mode != TMS_PQ_FAST && mode != TMS_PQ_EXACT) return TMS_ERR_INVALID;
+  if (mode != TMS_PQ_FAST && mode != TMS_PQ_EXACT && mode != TMS_PQ_PRECISE) return TMS_ERR_INVALID;
   if (n_queries < 0 || nq <= 0 || M <= 0 || K <= 0 || dsub <= 0 || n_docs < 0 || n_tokens < 0)
     return TMS_ERR_INVALID;
   if (q_dtype < TMS_F16 || q_dtype > TMS_F32 || cb_dtype < TMS_F16 || cb_dtype > TMS_F32)
@@ -420,14 +420,23 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // TMS_PQ_PRECISE with fp16 queries and one or two 32-row query chunks: the token-rows tensor
+  // kernel with the codebook split into fp16 hi + lo (the reference's precision); larger batches
+  // and other shapes take the table lookups below.
+  if (mode == TMS_PQ_PRECISE && q_dtype == TMS_F16) {
+    const int rc = pq_tokrows_maxsim(Q, n_queries, nq, codebook, cb_dtype, M, K, dsub, codes,
+                                     n_tokens, doc_offsets, n_docs, nd_uniform, out, workspace,
+                                     workspace_bytes, st, true);
+    if (rc != TMS_ERR_UNSUPPORTED) return rc;
+  }
   // Tensor-core path: codes decoded through a shared-memory fp16 codebook into MMA operand tiles
   // (fp16 queries, TMS_PQ_FAST); otherwise the exact fp32 table-lookup kernel below.
   if (mode == TMS_PQ_FAST && q_dtype == TMS_F16 && pq_mma_codebook_bytes(M, K, dsub)) {
-    // up to four 32-row query chunks: decoded tokens as the TMEM A operand (pq_tokrows.cu)
+    // up to two 32-row query chunks: decoded tokens as the TMEM A operand (pq_tokrows.cu)
     {
       const int rc = pq_tokrows_maxsim(Q, n_queries, nq, codebook, cb_dtype, M, K, dsub, codes,
                                        n_tokens, doc_offsets, n_docs, nd_uniform, out, workspace,
-                                       workspace_bytes, st);
+                                       workspace_bytes, st, false);
       if (rc != TMS_ERR_UNSUPPORTED) return rc;
     }
     const int rc = pq_mma_maxsim(Q, n_queries, nq, codebook, cb_dtype, M, K, dsub, codes, n_tokens,

@@ -100,13 +100,15 @@ __device__ __forceinline__ float xpose_max32(float (&v)[32]) {
   return v[0];
 }
 
-template <int NCH>
+template <int NCH, bool SPLIT>
 __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int N = NCH * 32;
-  const int acols = a.d / 2;  // TMEM columns of one decoded tile (fp16 pairs)
+  // TMEM columns of one decoded tile (fp16 pairs): d, or 2d for [hi | lo] rows
+  const int acols = a.d / 2 * (SPLIT ? 2 : 1);
   const int S = a.nslot;
-  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(a.M * a.K * a.dsub * 2), S);
+  const int n_cb = a.M * a.K * a.dsub;  // codebook elements (one table; the lo table follows)
+  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(n_cb * 2 * (SPLIT ? 2 : 1)), S);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t b_s = sbase + L.b_off;
   const uint32_t bar_s = sbase + L.bar_off;
@@ -179,7 +181,10 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       if (a.cb_dtype == TMS_F16) v = __half2float(reinterpret_cast<const __half*>(a.codebook)[i]);
       else if (a.cb_dtype == TMS_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.codebook)[i]);
       else v = reinterpret_cast<const float*>(a.codebook)[i];
-      cbs[i] = __float2half_rn(v);
+      const __half hi = __float2half_rn(v);
+      cbs[i] = hi;
+      // the rounding error of hi, itself rounded to fp16: hi + lo carries ~22 significant bits
+      if (SPLIT) cbs[n + i] = __float2half_rn(v - __half2float(hi));
     }
     const int upr = a.d / 8;  // 16-byte units per query row
     for (int i = threadIdx.x; i < N * upr; i += blockDim.x) {
@@ -221,8 +226,11 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
         const int s = j % S;
         if (!mbar_wait(afull_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 21)) break;
         tc_fence_after();
-        for (int k = 0; k < a.d / 16; ++k) {
-          const uint64_t bd = sw128_kmajor_desc(b_s + static_cast<uint32_t>((k >> 2) * N * 128 + (k & 3) * 32));
+        // split codebook: K runs over [hi | lo] columns of A against the query rows twice
+        const int kd = a.d / 16;
+        for (int k = 0; k < acols / 8; ++k) {
+          const int kq = (SPLIT && k >= kd) ? k - kd : k;
+          const uint64_t bd = sw128_kmajor_desc(b_s + static_cast<uint32_t>((kq >> 2) * N * 128 + (kq & 3) * 32));
           mma_f16_ts(tmem_base + acc_col(s), tmem_base + a_col(s) + 8u * k, bd, idesc, k != 0);
         }
         mma_commit(accf_bar(s));
@@ -261,14 +269,19 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
       const int64_t tok = lo + 32LL * j + lane;
       const bool valid = tok < hi;
-      for (int h = hp; h < a.d / 64; h += 2) {
+      const int hblocks = a.d / 64;
+      for (int h = hp; h < hblocks * (SPLIT ? 2 : 1); h += 2) {
+        // block h of the decoded row: column block hh of the hi table, or of the lo table
+        const bool lo_half = SPLIT && h >= hblocks;
+        const int hh = lo_half ? h - hblocks : h;
+        const __half* tab = lo_half ? cbs + n_cb : cbs;
         uint32_t r[32];
         if (fast) {  // h == hp: subspaces 8 hp .. 8 hp + 7
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             uint32_t code = ((i < 4 ? cc.x : cc.y) >> (8 * (i & 3))) & 0xffu;
             code = min(code, kmax);  // never read past the codebook
-            const uint4 e = *reinterpret_cast<const uint4*>(cbs + ((8 * hp + i) * a.K + code) * 8);
+            const uint4 e = *reinterpret_cast<const uint4*>(tab + ((8 * hp + i) * a.K + code) * 8);
             r[4 * i] = valid ? e.x : 0u;
             r[4 * i + 1] = valid ? e.y : 0u;
             r[4 * i + 2] = valid ? e.z : 0u;
@@ -277,12 +290,12 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const int col = 8 * (8 * h + i);  // first element of this 16-byte unit
+            const int col = 8 * (8 * hh + i);  // first element of this 16-byte unit
             const int m = col / a.dsub, part = col - m * a.dsub;
             uint4 e = make_uint4(0, 0, 0, 0);
             if (valid) {
               const uint32_t code = min(static_cast<uint32_t>(__ldg(a.codes + tok * a.M + m)), kmax);
-              e = *reinterpret_cast<const uint4*>(cbs + (m * a.K + code) * a.dsub + part);
+              e = *reinterpret_cast<const uint4*>(tab + (m * a.K + code) * a.dsub + part);
             }
             r[4 * i] = e.x;
             r[4 * i + 1] = e.y;
@@ -426,19 +439,20 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
                       int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
                       int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
                       int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
-                      cudaStream_t st) {
+                      cudaStream_t st, bool split) {
   const int64_t d = M * dsub;
   const int64_t nchunk = (nq + 31) / 32;
   const int64_t chunks = n_queries * nchunk;
-  const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2;
+  const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
   if (chunks < 1 || chunks > kTrMaxChunks || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
-      K > 256 || cb_bytes > 96 * 1024 || n_tokens <= 0 || (reinterpret_cast<uintptr_t>(Q) & 15))
+      K > 256 || cb_bytes > (split ? 128 : 96) * 1024 || n_tokens <= 0 ||
+      (reinterpret_cast<uintptr_t>(Q) & 15))
     return TMS_ERR_UNSUPPORTED;
   int status = TMS_OK;
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
   const int N = static_cast<int>(chunks) * 32;
-  const int acols = static_cast<int>(d / 2);
+  const int acols = static_cast<int>(d / 2) * (split ? 2 : 1);
   // as many slots as TMEM holds: a hand-off through an mbarrier takes ~500 cycles, so several
   // tiles must be in flight between the decoders, the MMA and the epilogue
   int nslot = 512 / (acols + N);
@@ -481,7 +495,8 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   const size_t half = static_cast<size_t>(dev->max_smem_optin) / 2 + 1024;
   if (smem < half) smem = half;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
-  auto kern = (chunks == 1) ? pq_tokrows_kernel<1> : pq_tokrows_kernel<2>;
+  auto kern = split ? ((chunks == 1) ? pq_tokrows_kernel<1, true> : pq_tokrows_kernel<2, true>)
+                    : ((chunks == 1) ? pq_tokrows_kernel<1, false> : pq_tokrows_kernel<2, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return TMS_ERR_CUDA;

@@ -59,14 +59,15 @@ int pq_mma_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* code
                   const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
                   void* workspace, size_t workspace_bytes, cudaStream_t st);
 
-// Tensor-core PQ path for small query batches (<= 4 chunks of 32 query rows), tokens on the TMEM
-// lanes; defined in pq_tokrows.cu. Q is fp16. Returns TMS_ERR_UNSUPPORTED for shapes it does not
-// take.
+// Tensor-core PQ path for small query batches (<= 2 chunks of 32 query rows), tokens on the TMEM
+// lanes; defined in pq_tokrows.cu. Q is fp16. `split`: the codebook as fp16 hi + fp16 lo (about 22
+// significant bits, the fp32 reference's precision) instead of rounded to fp16. Returns
+// TMS_ERR_UNSUPPORTED for shapes it does not take.
 size_t pq_tokrows_workspace_size(int64_t n_queries, int64_t nq, int64_t n_docs);
 int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook,
                       int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
                       int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
                       int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
-                      cudaStream_t st);
+                      cudaStream_t st, bool split);
 
 }  // namespace tms

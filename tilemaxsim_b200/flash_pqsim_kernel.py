@@ -5,9 +5,13 @@ methods (``build_distance_table``, ``score_batch``, ``score_single``; src/flash_
 176-280). Scoring goes through the C ABI ``tms_pq_maxsim`` and reads the uint8 codes directly:
 neither the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (the reference wrote
 both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default
-(``exact=True``) scoring keeps the reference's arithmetic: each CTA builds an fp32 distance table
-for eight query tokens in shared memory and sums table entries straight from the uint8 codes (no
-reconstruction), agreeing with the reference's ADC path to fp32 rounding (1e-5 relative).
+(``exact=True``) scoring keeps the reference's precision, agreeing with its ADC path to fp32
+rounding (1e-5 relative): each CTA builds an fp32 distance table for eight query tokens in shared
+memory and sums table entries straight from the uint8 codes (no reconstruction); one or two fp16
+queries of up to 32 tokens (one of up to 64) instead run on the tensor cores with each token
+rebuilt from the codebook split into fp16 hi + fp16 lo parts, which carry about 22 significant
+bits (the codebook must lie inside the fp16 range, checked at construction; otherwise the table
+lookups take every shape).
 ``exact=False`` is the faster tensor-core mode: queries in fp16 (fp32 / bf16 ones are rounded to
 fp16) and each token rebuilt on chip from an fp16 copy of the codebook; for one or two 32-row query
 chunks the rebuilt tokens go to tensor memory as the MMA's A operand (token-rows kernel), for
@@ -44,6 +48,9 @@ class TileMaxSimPQ:
         fall back to the table lookups."""
         self.exact = bool(exact)
         self.codebook = codebook.contiguous()
+        # the tensor-core route to the reference's precision stores the codebook as fp16 hi + lo,
+        # which needs every centroid value inside the fp16 range (checked once here)
+        self._split_ok = bool(self.codebook.abs().max().item() < 65504.0) if self.codebook.numel() else False
         self.M, self.K, self.dsub = codebook.shape
         self.d = self.M * self.dsub
         if self.codebook.dtype not in _lib.DTYPE_CODE:
@@ -104,12 +111,17 @@ class TileMaxSimPQ:
                 ctypes.c_void_p(self.codebook.data_ptr()), _lib.DTYPE_CODE[self.codebook.dtype],
                 self.M, self.K, self.dsub, ctypes.c_void_p(codes_tokens.data_ptr()), codes_tokens.shape[0],
                 ctypes.c_void_p(offsets.data_ptr() if offsets is not None else 0), n_docs, nd,
-                ctypes.c_void_p(out.data_ptr()), _lib.TMS_PQ_EXACT if self.exact else _lib.TMS_PQ_FAST,
+                ctypes.c_void_p(out.data_ptr()), self._mode(),
                 ctypes.c_void_p(ws_ptr), ws_bytes,
                 ctypes.c_void_p(_lib.stream_handle(dev)))
             _lib.check(rc, "tms_pq_maxsim")
             del ws
         return out
+
+    def _mode(self) -> int:
+        if not self.exact:
+            return _lib.TMS_PQ_FAST
+        return _lib.TMS_PQ_PRECISE if self._split_ok else _lib.TMS_PQ_EXACT
 
     def score_batch(self, Q: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:
         """(Nq, d) query vs (B, Nd, M) codes -> (B,) fp32 (reference: src/flash_pqsim_kernel.py:213-252)."""
