@@ -354,16 +354,28 @@ PQ_CONFIGS = {
 PQ_CONFIGS.update({f"{k}_fast": v for k, v in list(PQ_CONFIGS.items())})
 
 
-def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> int:
-    """Kernels one PQ scoring call launches (csrc/pq_adc.cu routing). Exact mode: the table-lookup
-    kernel, plus the slice sum when Nq > 8. Fast mode: the token-rows kernel for 1-2 query chunks,
-    else query packing + the decoder-warp dense kernel; plus the chunk sum when Nq > 32."""
-    if exact:
-        return 1 + (1 if nq > 8 else 0)
+def pq_route(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> str:
+    """The kernel tms_pq_maxsim picks for fp16 queries (csrc/pq_adc.cu routing): "tokrows" (the
+    token-rows tensor kernel; codebook split into hi + lo at the default precision) for 1-2 chunks of
+    32 query rows, else "lut" (table lookups) at the default precision or "decoder" (the dense
+    kernel's decoder warps) in fast mode."""
     chunks = nqry * -(-nq // 32)
     d = M * dsub
-    tokrows = chunks <= 2 and d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256
-    return (1 if tokrows else 2) + (1 if nq > 32 else 0)
+    cb = M * K * dsub * 2 * (2 if exact else 1)
+    if chunks <= 2 and d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256 and \
+            cb <= (128 if exact else 96) * 1024:
+        return "tokrows"
+    return "lut" if exact else "decoder"
+
+
+def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> int:
+    """Kernels one PQ scoring call launches: the scoring kernel (+ query packing for the decoder
+    kernel) and the partial-sum kernel when a query spans several slices (8 query tokens per table
+    slice, 32 per tensor chunk)."""
+    route = pq_route(nqry, nq, M, K, dsub, exact)
+    if route == "lut":
+        return 1 + (1 if nq > 8 else 0)
+    return (1 if route == "tokrows" else 2) + (1 if nq > 32 else 0)
 
 
 def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = True) -> dict | None:
@@ -444,7 +456,8 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = 
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     hbm = {"achieved_gbs": code_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": pk["hbm_gbs"],
            "frac": code_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
-    if exact:
+    route = pq_route(nqry, nq, M, K, dsub, exact)
+    if route == "lut":
         # table lookups: one fp32 entry per (query token, doc token, subspace), read from shared
         # memory; the port moves 128 B per clock per SM = 32 conflict-free 4-byte lookups
         lk_peak = 32.0 * sms * mhz * 1e6
@@ -454,10 +467,12 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = 
                 "note": "fp32 table lookups straight from uint8 codes (reference arithmetic); peak = "
                         "32 lookups/clk/SM (the 128 B/clk shared-memory port) x SMs x median SM clock"}
     else:
-        flops = 2.0 * nqry * nq * T * M * dsub
+        flops = 2.0 * nqry * nq * T * M * dsub * (2 if exact else 1)  # MMA work (hi and lo halves)
         tmem_bytes = 4.0 * nqry * nq * T
         tmem_peak = 56.0 * sms * mhz * 1e6 / 1e9
-        gather_bytes = float(T) * M * dsub * 2
+        # decoding reads one codebook row (dsub fp16) per code from shared memory -- two (hi and lo)
+        # at the default precision
+        gather_bytes = float(T) * M * dsub * 2 * (2 if exact else 1)
         smem_peak = 128.0 * sms * mhz * 1e6 / 1e9
         # codes decoded in shared memory, MMA on the tensor cores, the epilogue reading every fp32
         # similarity from TMEM (B_q*Nq*T values) -- the same bound as the dense kernel
@@ -471,15 +486,17 @@ def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = 
                 # T*M*dsub*2 bytes per launch at least, against 128 B/clk per SM
                 "smem_gather": {"achieved_gbs": gather_bytes / (kern_ms * 1e-3) / 1e9, "peak_gbs": smem_peak,
                                 "frac": gather_bytes / (kern_ms * 1e-3) / 1e9 / smem_peak},
-                "note": "codebook rounded to fp16 (exact=False); LUT lookups/s counts the table-lookup "
-                        "equivalent (B_q*Nq*T*M) of the work"}
+                "note": ("codebook split into fp16 hi + lo (reference precision), " if exact else
+                         "codebook rounded to fp16 (exact=False), ") + f"{route} kernel; LUT lookups/s "
+                        "counts the table-lookup equivalent (B_q*Nq*T*M) of the work"}
     out = {
         "metric": "doc-tokens scored/s", "value": pairs / (ms * 1e-3), "unit": "doc-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": f"{args.config}: PQ-ADC, {nqry} queries x {nq} tokens vs {n_docs} docs x {nd} "
                                f"uint8 codes per GPU (M={M}, K={K}, dsub={dsub}, fp32 codebook), top-{k}, "
-                               + ("fp32 table lookups (reference precision)" if exact
+                               + ("reference precision (" + ("hi/lo tensor cores" if route == "tokrows"
+                                                            else "fp32 table lookups") + ")" if exact
                                   else "tensor-core mode (fp16 codebook)"),
                    "l2": "codes larger than L2"},
         "queries_per_s": nqry / (ms * 1e-3), "pq_kernel_ms": kern_ms,
