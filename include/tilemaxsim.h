@@ -231,6 +231,16 @@ TMS_API int tms_mask_candidates(float* scores, int64_t n_queries, int64_t n_cand
                                 const int64_t* ids, const uint32_t* bitmaps, int64_t n_docs,
                                 float fill, void* stream);
 
+/* Sharded search merge (no reference function: the reference has no distributed path). Each rank
+ * packs its (rows, k) list into packed (rows, 2k) int64: k ids, then the k scores' fp32 bit
+ * patterns; after an all-gather of the packed rows (rank-major: (world * rows, 2k)),
+ * tms_topk_merge_packed writes the global top-k of every row by the tms_topk rule (score
+ * descending, id ascending, NaN last). world * k <= 16384. */
+TMS_API int tms_topk_pack(const float* vals, const int64_t* ids, int64_t rows, int64_t k,
+                          int64_t* packed, void* stream);
+TMS_API int tms_topk_merge_packed(const int64_t* gathered, int64_t world, int64_t rows, int64_t k,
+                                  float* out_vals, int64_t* out_ids, void* stream);
+
 /* ---------------------------------------------------------------- introspection and test hooks */
 
 /* Launch plan the dense kernel would use (no reference counterpart): info[0..9] = tokens per tile,

@@ -263,3 +263,33 @@ def test_pq_precise_tensor_path_vs_oracle(nqry, nq, lengths, cuda_device):
     inf = np.isinf(want)
     np.testing.assert_array_equal(got[inf], want[inf])
     np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("world,rows,k", [(3, 5, 100), (8, 64, 1000), (2, 3, 7)])
+def test_packed_merge_equals_topk_of_candidates(world, rows, k, cuda_device):
+    """The shard merge's pack and merge kernels, with the all-gather emulated on one GPU (ranks'
+    packed rows concatenated rank-major): equal to the oracle's top-k of all ranks' candidates,
+    ties (many) and NaN padding included."""
+    import ctypes
+    from tilemaxsim_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(world * rows + k)
+    vals = (torch.randint(0, 50, (world, rows, k), generator=g).float() / 4.0)
+    vals[:, :, -2:] = float("nan")  # padded lists
+    ids = torch.randint(0, 10**12, (world, rows, k), generator=g)
+    packed = torch.empty(world, rows, 2 * k, dtype=torch.int64, device=cuda_device)
+    vd, idd = vals.to(cuda_device), ids.to(cuda_device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for r in range(world):
+        assert lib.tms_topk_pack(ctypes.c_void_p(vd[r].data_ptr()), ctypes.c_void_p(idd[r].data_ptr()), rows, k,
+                                 ctypes.c_void_p(packed[r].data_ptr()), stream) == 0
+    out_v = torch.empty(rows, k, device=cuda_device)
+    out_i = torch.empty(rows, k, dtype=torch.int64, device=cuda_device)
+    assert lib.tms_topk_merge_packed(ctypes.c_void_p(packed.data_ptr()), world, rows, k,
+                                     ctypes.c_void_p(out_v.data_ptr()), ctypes.c_void_p(out_i.data_ptr()),
+                                     stream) == 0
+    cand_v = vals.permute(1, 0, 2).reshape(rows, world * k)
+    cand_i = ids.permute(1, 0, 2).reshape(rows, world * k)
+    wv, wi = O.topk(cand_v.numpy(), k, ids=cand_i.numpy())
+    np.testing.assert_array_equal(out_i.cpu().numpy(), wi)
+    np.testing.assert_array_equal(out_v.cpu().numpy(), wv)

@@ -38,6 +38,8 @@ SIGNATURES = {
     "tms_set_debug": (None, [_u64, _i32]),
     "tms_validate_offsets": (_i32, [_vp, _i64, _i64, _vp]),
     "tms_dense_workspace_size": (_sz, [_i32, _i64, _i64, _i64, _i64, _i32]),
+    "tms_topk_pack": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "tms_topk_merge_packed": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "tms_ivf_candidates": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "tms_gather_offsets": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp]),
     "tms_gather_docs": (_i32, [_vp, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),

@@ -91,6 +91,48 @@ __global__ void __launch_bounds__(kTopkThreads)
   }
 }
 
+// Shard merge without unpacking: every rank's (rows, k) list is packed as one int64 row of 2k
+// entries (k ids, then the k scores' fp32 bit patterns), all-gathered rank-major, and merged here:
+// one CTA per query row reads its world * k candidates straight from the gathered buffer.
+__global__ void pack_topk_kernel(const float* __restrict__ vals, const int64_t* __restrict__ ids,
+                                 int64_t rows, int64_t k, int64_t* __restrict__ packed) {
+  const int64_t total = rows * k;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / k, j = e - r * k;
+    packed[r * 2 * k + j] = ids[e];
+    packed[r * 2 * k + k + j] = static_cast<int64_t>(__float_as_uint(vals[e]));
+  }
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+    merge_packed_topk_kernel(const int64_t* __restrict__ gathered, int world, int64_t rows, int k,
+                             float* __restrict__ out_vals, int64_t* __restrict__ out_ids) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int n = world * k;
+  const int P = next_pow2(n);
+  int64_t* ids = reinterpret_cast<int64_t*>(sm);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sm + static_cast<size_t>(P) * 8);
+  const int64_t row = blockIdx.x;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    if (i < n) {
+      const int r = i / k, j = i - r * k;
+      const int64_t* src = gathered + (static_cast<int64_t>(r) * rows + row) * 2 * k;
+      keys[i] = f2key(__uint_as_float(static_cast<uint32_t>(src[k + j])));
+      ids[i] = src[j];
+    } else {
+      keys[i] = 0u;
+      ids[i] = INT64_MAX;
+    }
+  }
+  __syncthreads();
+  bitonic_sort(keys, ids, P);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    out_vals[row * k + i] = key2f(keys[i]);
+    out_ids[row * k + i] = ids[i];
+  }
+}
+
 __global__ void __launch_bounds__(kTopkThreads)
     topk_select_kernel(const float* __restrict__ scores, int64_t n, int64_t ld, int k,
                        int64_t id_base, float* __restrict__ out_vals,
@@ -285,5 +327,39 @@ extern "C" int tms_topk(const float* scores, int64_t rows, int64_t n, int64_t ld
   }
   topk_select_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, st>>>(
       scores, n, ld, static_cast<int>(k), id_base, out_vals, out_ids, n, 1);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int tms_topk_pack(const float* vals, const int64_t* ids, int64_t rows, int64_t k,
+                             int64_t* packed, void* stream) {
+  NvtxRange nvtx_range("tms_topk_pack");
+  if (rows < 0 || k < 0) return TMS_ERR_INVALID;
+  if (rows * k == 0) return TMS_OK;
+  if (!vals || !ids || !packed) return TMS_ERR_INVALID;
+  int status = TMS_OK;
+  const DeviceInfo* dev = current_device_info(&status);
+  if (!dev) return status;
+  int blocks = static_cast<int>((rows * k + 255) / 256);
+  if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
+  pack_topk_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(vals, ids, rows, k, packed);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int tms_topk_merge_packed(const int64_t* gathered, int64_t world, int64_t rows, int64_t k,
+                                     float* out_vals, int64_t* out_ids, void* stream) {
+  NvtxRange nvtx_range("tms_topk_merge_packed");
+  if (world < 1 || rows < 0 || k < 0) return TMS_ERR_INVALID;
+  if (rows * k == 0) return TMS_OK;
+  if (!gathered || !out_vals || !out_ids) return TMS_ERR_INVALID;
+  if (world * k > kSortMax || rows > 0x7fffffffLL) return TMS_ERR_UNSUPPORTED;
+  int P = 1;
+  while (P < world * k) P <<= 1;
+  const size_t smem = static_cast<size_t>(P) * 12;
+  if (cudaFuncSetAttribute(merge_packed_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return TMS_ERR_CUDA;
+  merge_packed_topk_kernel<<<static_cast<unsigned>(rows), kTopkThreads, smem,
+                             static_cast<cudaStream_t>(stream)>>>(
+      gathered, static_cast<int>(world), rows, static_cast<int>(k), out_vals, out_ids);
   return cuda_status(cudaGetLastError());
 }

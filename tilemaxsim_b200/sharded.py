@@ -13,11 +13,13 @@ process with no merge, src/run_all_experiments.py:355-443); this is additive API
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .maxsim import maxsim_batched, topk
 
 PAD_ID = torch.iinfo(torch.int64).max
@@ -40,19 +42,36 @@ def merge_topk(vals: torch.Tensor, ids: torch.Tensor, k: int, group=None,
                topk_fn: Callable | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Merges every rank's (rows, k) top-k list into the global (rows, k) top-k.
 
-    `topk_fn(scores, k, ids=...)` ranks the gathered candidates; it defaults to the library's GPU
-    top-k (the CPU tests pass the oracle's)."""
+    One all-gather of a packed (rows, 2k) int64 buffer per rank (the k global ids, then the k
+    scores' fp32 bit patterns). On CUDA tensors the library packs (`tms_topk_pack`) and merges
+    straight from the gathered buffer (`tms_topk_merge_packed`, the tms_topk rule); `topk_fn(scores,
+    k, ids=...)` replaces that merge (the CPU tests pass the oracle's) and then the candidates are
+    unpacked with torch."""
     vals, ids = _pad_to_k(vals, ids, k)
     if group is None or dist.get_world_size(group) == 1:
         return vals, ids
     world = dist.get_world_size(group)
     rows = vals.shape[0]
-    # one collective: ids and the scores' bit patterns travel in one int64 buffer (rows, 2k)
+    native = topk_fn is None and vals.is_cuda
     packed = torch.empty((rows, 2 * k), dtype=torch.int64, device=vals.device)
-    packed[:, :k] = ids
-    packed[:, k:] = vals.view(torch.int32).to(torch.int64)
+    if native:
+        lib = _lib.load()
+        stream = ctypes.c_void_p(_lib.stream_handle(vals.device))
+        _lib.check(lib.tms_topk_pack(ctypes.c_void_p(vals.data_ptr()), ctypes.c_void_p(ids.data_ptr()),
+                                     rows, k, ctypes.c_void_p(packed.data_ptr()), stream), "tms_topk_pack")
+    else:
+        packed[:, :k] = ids
+        packed[:, k:] = vals.view(torch.int32).to(torch.int64)
     gathered = torch.empty((world * rows, 2 * k), dtype=torch.int64, device=vals.device)
     dist.all_gather_into_tensor(gathered, packed, group=group)  # rank-major along dim 0
+    if native:
+        out_v = torch.empty((rows, k), dtype=torch.float32, device=vals.device)
+        out_i = torch.empty((rows, k), dtype=torch.int64, device=vals.device)
+        _lib.check(lib.tms_topk_merge_packed(ctypes.c_void_p(gathered.data_ptr()), world, rows, k,
+                                             ctypes.c_void_p(out_v.data_ptr()),
+                                             ctypes.c_void_p(out_i.data_ptr()), stream),
+                   "tms_topk_merge_packed")
+        return out_v, out_i
     g = gathered.view(world, rows, 2 * k).permute(1, 0, 2)  # (rows, world, 2k)
     cand_i = g[:, :, :k].reshape(rows, world * k)
     cand_v = g[:, :, k:].reshape(rows, world * k).to(torch.int32).view(torch.float32)
