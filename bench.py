@@ -349,6 +349,7 @@ PQ_CONFIGS = {
     "c4_small": (16, 32, 16, 256, 8, 50_000, 128, 100),
     # single-query PQ over the same corpus (the north star's single-query PQ path)
     "q1_pq": (1, 32, 16, 256, 8, 1_000_000, 128, 100),
+    "q1_pq_small": (1, 32, 16, 256, 8, 100_000, 128, 100),  # ncu captures (205 MB of codes)
 }
 # the same workloads on the tensor-core mode (exact=False: codebook rounded to fp16, ~1e-3 relative)
 PQ_CONFIGS.update({f"{k}_fast": v for k, v in list(PQ_CONFIGS.items())})
