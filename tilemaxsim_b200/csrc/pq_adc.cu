@@ -244,28 +244,23 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
   auto lookup = [&](int aa, uint32_t off) -> float {
     return *reinterpret_cast<const float*>(tb + static_cast<uint32_t>((aa >> 1) * K * 256 + (aa & 1) * 128) + off);
   };
-  // lane group g reads only its own A code bytes of a token: one 4-byte (M = 16) or 2-byte
-  // (M = 8) load, four different tokens per warp instruction inside one 64-byte span
+  // Codes are staged per warp in shared memory, 32 tokens at a time: lane l loads token l's whole
+  // code row with one coalesced load (the next 32 rows are in flight in registers meanwhile), and
+  // lane group g then reads only its own A code bytes of a token (one 4-byte or 2-byte shared
+  // load; the four groups read four tokens' words in distinct banks).
   using CodeWord = typename std::conditional<A == 4, uint32_t, uint16_t>::type;
+  using CodeRow = typename std::conditional<A == 4, uint4, uint2>::type;
+  CodeRow* const stage = reinterpret_cast<CodeRow*>(tbl4 + A * K * 32) + warp * 32;
+  const CodeWord* const stage_w = reinterpret_cast<const CodeWord*>(stage) + g;
 
   for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
     // clamped to the code rows that exist, so malformed offsets never read outside `codes`
     const int64_t t_lo = max(min(a.docs.start(doc), a.n_tokens), int64_t(0));
     const int64_t t_hi = max(min(a.docs.start(doc + 1), a.n_tokens), t_lo);
     const int len = static_cast<int>(min(t_hi - t_lo, int64_t(0x7fffffff)));
-    const CodeWord* words = reinterpret_cast<const CodeWord*>(a.codes + t_lo * (4 * A)) + g;
+    const CodeRow* rows = reinterpret_cast<const CodeRow*>(a.codes + t_lo * (4 * A));
     float run = kNegInfPq;
-    // Lane group g handles each group of four tokens in the order j0 + (t ^ g): after the
-    // reduce-scatter below its own token j0 + g then needs no select. A step takes eight tokens
-    // (two independent groups of four); the codes of the next step are in flight meanwhile.
     const int last = len - 1;
-    auto load8 = [&](int j0, uint32_t (&c)[8], bool clamp) {
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const int j = j0 + (t & 4) + ((t & 3) ^ g);
-        c[t] = __ldg(words + 4 * (clamp ? min(j, last) : j));
-      }
-    };
     // the full sum of token j0 + g from this lane's partial sums p[t] of tokens j0 + (t ^ g):
     // the partner g ^ 2 holds j0 + g (its t = 2) and j0 + (1 ^ g) (its t = 3); then g ^ 1 holds
     // j0 + g as its t = 1
@@ -274,40 +269,41 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
       const float q1 = p[1] + __shfl_xor_sync(0xffffffffu, p[3], 16);
       return q0 + __shfl_xor_sync(0xffffffffu, q1, 8);
     };
-    auto step = [&](const uint32_t (&c)[8], int j0, bool tail) {
+    // eight tokens c0 + s0 .. c0 + s0 + 7 from the staged rows (s0 = their position in the stage);
+    // lane group g handles each group of four in the order (t ^ g)
+    auto step = [&](int s0, int j0, bool tail) {
       float p[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        float acc = lookup(0, row_off(c[t], 0));
+        const uint32_t c = stage_w[(s0 + (t & 4) + ((t & 3) ^ g)) * 4];
+        float acc = lookup(0, row_off(c, 0));
 #pragma unroll
-        for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(c[t], aa));
+        for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(c, aa));
         p[t] = acc;
       }
-      const float s0 = reduce4(p), s1 = reduce4(p + 4);
+      const float s0v = reduce4(p), s1v = reduce4(p + 4);
       if (!tail) {
-        run = fmax3(run, s0, s1);
+        run = fmax3(run, s0v, s1v);
       } else {
-        if (j0 + g < len) run = fmaxf(run, s0);
-        if (j0 + 4 + g < len) run = fmaxf(run, s1);
+        if (j0 + g < len) run = fmaxf(run, s0v);
+        if (j0 + 4 + g < len) run = fmaxf(run, s1v);
       }
     };
     if (len > 0) {
-      uint32_t nxt[8];
-      load8(0, nxt, true);
-      int j0 = 0;
-      for (; j0 + 16 <= len; j0 += 8) {  // this step and the next are whole: no clamping
-        uint32_t cur[8];
+      CodeRow nxt = __ldg(rows + min(lane, last));
+      for (int c0 = 0; c0 < len; c0 += 32) {
+        const CodeRow cur = nxt;
+        if (c0 + 32 < len) nxt = __ldg(rows + min(c0 + 32 + lane, last));
+        __syncwarp();
+        stage[lane] = cur;
+        __syncwarp();
+        const int n = min(32, len - c0);
+        if (n == 32) {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) cur[t] = nxt[t];
-        load8(j0 + 8, nxt, false);
-        step(cur, j0, false);
-      }
-      for (; j0 < len; j0 += 8) {
-        uint32_t cur[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) cur[t] = nxt[t];
-        load8(j0 + 8, nxt, true);
-        step(cur, j0, j0 + 8 > len);
+          for (int s0 = 0; s0 < 32; s0 += 8) step(s0, c0 + s0, false);
+        } else {
+          for (int s0 = 0; s0 < n; s0 += 8) step(s0, c0 + s0, s0 + 8 > n);
+        }
       }
     }
     run = fmaxf(run, __shfl_xor_sync(0xffffffffu, run, 8));
@@ -448,7 +444,9 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   const bool lut4 = (M == 16 || M == 8) && (reinterpret_cast<uintptr_t>(codes) % M) == 0 &&
                     M * K * 32 <= kPqTableBudget;
   const int qs = lut4 ? 8 : pick_qs(M, K, nq);
-  const size_t smem = static_cast<size_t>(M * K * (lut4 ? 32 : qs)) * (lut4 ? 1 : 4);
+  // lut4: the table plus one 32-row code stage per warp
+  const size_t smem = lut4 ? static_cast<size_t>(M * K * 32) + (kLut4Threads / 32) * 32 * M
+                           : static_cast<size_t>(M * K * qs) * 4;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
   const int nslice = static_cast<int>((nq + qs - 1) / qs);
   const size_t need = nslice > 1 ? static_cast<size_t>(n_queries * nslice * n_docs) * 4 : 0;
