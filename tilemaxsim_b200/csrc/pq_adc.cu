@@ -245,13 +245,24 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
     return *reinterpret_cast<const float*>(tb + static_cast<uint32_t>((aa >> 1) * K * 256 + (aa & 1) * 128) + off);
   };
   // Codes are staged per warp in shared memory, 32 tokens at a time: lane l loads token l's whole
-  // code row with one coalesced load (the next 32 rows are in flight in registers meanwhile), and
-  // lane group g then reads only its own A code bytes of a token (one 4-byte or 2-byte shared
-  // load; the four groups read four tokens' words in distinct banks).
+  // code row with one coalesced load (the next 32 rows are in flight in registers meanwhile) and
+  // stores it transposed, word g (code bytes A g .. A g + A - 1) into row g of the stage (rows 36
+  // words apart, so the four rows start in different banks). Lane group g then reads its words of
+  // four consecutive tokens with one vector load.
   using CodeWord = typename std::conditional<A == 4, uint32_t, uint16_t>::type;
   using CodeRow = typename std::conditional<A == 4, uint4, uint2>::type;
-  CodeRow* const stage = reinterpret_cast<CodeRow*>(tbl4 + A * K * 32) + warp * 32;
-  const CodeWord* const stage_w = reinterpret_cast<const CodeWord*>(stage) + g;
+  using Word4 = typename std::conditional<A == 4, uint4, uint2>::type;  // 4 tokens' words
+  constexpr int kStagePitch = 36 * 4 / A;  // CodeWords per stage row (144 bytes)
+  CodeWord* const stage = reinterpret_cast<CodeWord*>(tbl4 + A * K * 32) + warp * 4 * kStagePitch;
+  const Word4* const stage_g = reinterpret_cast<const Word4*>(stage + g * kStagePitch);
+  auto word_of = [](const Word4& w, int u) -> uint32_t {  // token u's word of a 4-token vector
+    if constexpr (A == 4) return u == 0 ? w.x : u == 1 ? w.y : u == 2 ? w.z : w.w;
+    else return ((u < 2 ? w.x : w.y) >> (16 * (u & 1))) & 0xffffu;
+  };
+  auto row_word = [](const CodeRow& r, int gg) -> CodeWord {
+    if constexpr (A == 4) return gg == 0 ? r.x : gg == 1 ? r.y : gg == 2 ? r.z : r.w;
+    else return static_cast<CodeWord>(((gg < 2 ? r.x : r.y) >> (16 * (gg & 1))) & 0xffffu);
+  };
 
   for (int64_t doc = doc_begin + warp; doc < doc_end; doc += n_warps) {
     // clamped to the code rows that exist, so malformed offsets never read outside `codes`
@@ -272,13 +283,30 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
     // eight tokens c0 + s0 .. c0 + s0 + 7 from the staged rows (s0 = their position in the stage);
     // lane group g handles each group of four in the order (t ^ g)
     auto step = [&](int s0, int j0, bool tail) {
+      // c[t] = this group's word of token s0 + (t & 4) + ((t & 3) ^ g): the XOR order as two
+      // conditional pair swaps of the loaded words
+      uint32_t c[8];
+#pragma unroll
+      for (int h = 0; h < 8; h += 4) {
+        const Word4 w = stage_g[(s0 + h) / 4];
+        uint32_t v[4] = {word_of(w, 0), word_of(w, 1), word_of(w, 2), word_of(w, 3)};
+        if (g & 1) {
+          const uint32_t t0 = v[0], t2 = v[2];
+          v[0] = v[1]; v[1] = t0; v[2] = v[3]; v[3] = t2;
+        }
+        if (g & 2) {
+          const uint32_t t0 = v[0], t1 = v[1];
+          v[0] = v[2]; v[1] = v[3]; v[2] = t0; v[3] = t1;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) c[h + u] = v[u];
+      }
       float p[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        const uint32_t c = stage_w[(s0 + (t & 4) + ((t & 3) ^ g)) * 4];
-        float acc = lookup(0, row_off(c, 0));
+        float acc = lookup(0, row_off(c[t], 0));
 #pragma unroll
-        for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(c, aa));
+        for (int aa = 1; aa < A; ++aa) acc += lookup(aa, row_off(c[t], aa));
         p[t] = acc;
       }
       const float s0v = reduce4(p), s1v = reduce4(p + 4);
@@ -295,7 +323,8 @@ __global__ void __launch_bounds__(kLut4Threads, 1) pq_lut4_kernel(const PqArgs a
         const CodeRow cur = nxt;
         if (c0 + 32 < len) nxt = __ldg(rows + min(c0 + 32 + lane, last));
         __syncwarp();
-        stage[lane] = cur;
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) stage[gg * kStagePitch + lane] = row_word(cur, gg);
         __syncwarp();
         const int n = min(32, len - c0);
         if (n == 32) {
@@ -445,7 +474,7 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
                     M * K * 32 <= kPqTableBudget;
   const int qs = lut4 ? 8 : pick_qs(M, K, nq);
   // lut4: the table plus one 32-row code stage per warp
-  const size_t smem = lut4 ? static_cast<size_t>(M * K * 32) + (kLut4Threads / 32) * 32 * M
+  const size_t smem = lut4 ? static_cast<size_t>(M * K * 32) + (kLut4Threads / 32) * 4 * 144
                            : static_cast<size_t>(M * K * qs) * 4;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
   const int nslice = static_cast<int>((nq + qs - 1) / qs);
