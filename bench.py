@@ -360,12 +360,13 @@ def pq_route(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> str:
     token-rows tensor kernel; codebook split into hi + lo at the default precision) for 1-2 chunks of
     32 query rows, else "lut" (table lookups) at the default precision or "decoder" (the dense
     kernel's decoder warps) in fast mode."""
-    chunks = nqry * -(-nq // 32)
+    nchunk = -(-nq // 32)
+    chunks = nqry * nchunk
     d = M * dsub
     cb = M * K * dsub * 2 * (2 if exact else 1)
-    if chunks <= 2 and d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256 and \
-            cb <= (128 if exact else 96) * 1024:
-        return "tokrows"
+    shape_ok = d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256 and cb <= (128 if exact else 96) * 1024
+    if shape_ok and (chunks <= 2 or (exact and nchunk <= 2 and nq >= 17)):
+        return "tokrows"  # at the default precision: in passes of up to two chunks
     return "lut" if exact else "decoder"
 
 
@@ -376,7 +377,10 @@ def pq_score_launches(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool
     route = pq_route(nqry, nq, M, K, dsub, exact)
     if route == "lut":
         return 1 + (1 if nq > 8 else 0)
-    return (1 if route == "tokrows" else 2) + (1 if nq > 32 else 0)
+    if route == "tokrows":
+        passes = -(-nqry // (2 // -(-nq // 32))) if exact else 1
+        return passes * (1 + (1 if nq > 32 else 0))
+    return 2 + (1 if nq > 32 else 0)
 
 
 def run_pq(args, cfg, rank: int, world: int, device: torch.device, emit: bool = True) -> dict | None:
