@@ -241,10 +241,15 @@ def test_pq_exact_c4_full_size_document_independence(cuda_device):
 
 
 @pytest.mark.parametrize("nqry,nq,lengths", [(1, 32, "c4"), (2, 32, "c4"), (1, 64, "ragged"),
-                                              (2, 20, "ragged"), (1, 5, "tiny")])
+                                              (2, 20, "ragged"), (1, 5, "tiny"), (3, 32, "c4"),
+                                              (4, 32, "ragged"), (7, 16, "ragged"), (5, 40, "c4"),
+                                              (1, 128, "ragged"), (3, 100, "tiny"), (6, 8, "ragged")])
 def test_pq_precise_tensor_path_vs_oracle(nqry, nq, lengths, cuda_device):
-    """One or two fp16 queries at the default precision run on the tensor cores with the codebook
-    split into fp16 hi + lo: scores within 1e-5 relative of the reference's fp32 ADC arithmetic."""
+    """fp16 queries at the default precision run on the tensor cores with the codebook split into
+    fp16 hi + lo, in passes of up to four 32-row query chunks (three chunks on the four-chunk
+    kernel, partial last passes, 128-row queries); batches of <= 8-token queries needing several
+    passes take the fp32 table lookups. Scores within 1e-5 relative of the reference's fp32 ADC
+    arithmetic either way."""
     from tilemaxsim_b200 import TileMaxSimPQ, _lib
     if lengths == "c4":
         off = np.arange(2001, dtype=np.int64) * 128

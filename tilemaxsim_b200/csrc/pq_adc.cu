@@ -445,17 +445,15 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // TMS_PQ_PRECISE with fp16 queries and one or two 32-row query chunks: the token-rows tensor
-  // kernel with the codebook split into fp16 hi + lo (the reference's precision); larger batches
-  // and other shapes take the table lookups below.
-  // Larger batches of queries with at least 17 tokens run the same kernel in passes of up to two
-  // chunks (two queries of <= 32 tokens, or one of <= 64): a pass decodes the corpus once for
-  // its queries, while the table lookups cost ceil(Nq / 8) table slices per query -- at 32 tokens
-  // 16 queries take 92.7 ms in 8 passes against 173 ms of lookups (1M docs x 128 codes).
+  // TMS_PQ_PRECISE with fp16 queries of up to 128 rows: the token-rows tensor kernel with the
+  // codebook split into fp16 hi + lo (the reference's precision), in passes of up to four 32-row
+  // query chunks (four queries of <= 32 tokens, two of <= 64, one of <= 128). A pass decodes the
+  // corpus once for its queries, while the table lookups below cost ceil(Nq / 8) table slices per
+  // query, so batches of queries with <= 8 tokens that need more than one pass keep the lookups.
   const int64_t nchunk_q = (nq + 31) / 32;
-  if (mode == TMS_PQ_PRECISE && q_dtype == TMS_F16 && nchunk_q <= 2 &&
-      (n_queries * nchunk_q <= 2 || nq >= 17)) {
-    const int64_t per = 2 / nchunk_q;  // queries per pass
+  if (mode == TMS_PQ_PRECISE && q_dtype == TMS_F16 && nchunk_q <= 4 &&
+      (n_queries * nchunk_q <= 4 || nq >= 9)) {
+    const int64_t per = 4 / nchunk_q;  // queries per pass
     const int64_t d = M * dsub;
     int rc = TMS_OK;
     for (int64_t q0 = 0; q0 < n_queries && rc == TMS_OK; q0 += per) {

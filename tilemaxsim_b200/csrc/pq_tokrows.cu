@@ -1,5 +1,6 @@
 // pq_tokrows.cu -- PQ-ADC on the sm_100a tensor cores for small query batches (one or two
-// 32-row query chunks), with the document tokens on the TMEM lanes.
+// 32-row query chunks; up to four with the split codebook), with the document tokens on the TMEM
+// lanes.
 //
 //   score[q, doc] = sum_i max_{j in doc} sum_m <Q[q,i,m*dsub:(m+1)*dsub], C[m, codes[j,m], :]>
 //
@@ -27,9 +28,11 @@
 //  * A hand-off through an mbarrier costs ~500 cycles on this part, so TMEM holds as many tiles
 //    in flight as fit (5 at N = 32: 64 decoded-token columns + 32 accumulator columns each).
 //
-// Warp roles (512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 = decoders (lane
-// quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column blocks of every
-// tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only help in the prologue.
+// Warp roles (one or two chunks, 512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 =
+// decoders (lane quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column
+// blocks of every tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only
+// help in the prologue. Three or four chunks (codebook split only; 544 threads): warps 0..3 are a
+// second epilogue group and warp 16 is the MMA issuer (TrShape).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -40,10 +43,10 @@ namespace tms {
 
 namespace {
 
-constexpr int kTrThreads = 512;
 constexpr int kTrDecWarp0 = 4;
 constexpr int kTrEpiWarp0 = 12;
-constexpr int kTrMaxChunks = 2;  // N = 32 x chunks <= 64 query rows per CTA
+constexpr int kTrMaxChunks = 2;       // N = 32 x chunks <= 64 query rows per CTA
+constexpr int kTrMaxChunksSplit = 4;  // hi/lo rows: 128 query rows (two TMEM slots of 128 + 128)
 constexpr float kTrNegInf = -__builtin_huge_valf();
 
 struct TrArgs {
@@ -100,8 +103,49 @@ __device__ __forceinline__ float xpose_max32(float (&v)[32]) {
   return v[0];
 }
 
+// The first transposing step of xpose_max32 applied to one window r and max-merged into the
+// 16-value state acc: the step's outputs are maxima of fixed inputs, so max commutes with it and
+// the state of many windows finishes with xpose_max16. Halves the registers a chunk's running
+// maxima take. Lanes with in == false contribute -inf (tokens of another document).
+__device__ __forceinline__ void fold16(float (&acc)[16], const uint32_t (&r)[32], bool in) {
+  const bool up = (threadIdx.x & 16) != 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float send = in ? __uint_as_float(up ? r[i] : r[i + 16]) : kTrNegInf;
+    const float keep = in ? __uint_as_float(up ? r[i + 16] : r[i]) : kTrNegInf;
+    acc[i] = fmaxf(acc[i], fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16)));
+  }
+}
+// The remaining 15 shuffles of xpose_max32 on a state folded by fold16.
+__device__ __forceinline__ float xpose_max16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? v[i] : v[i + w];
+      const float keep = up ? v[i + w] : v[i];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
+    }
+  }
+  return v[0];
+}
+
+// Block shape per query-chunk count. Up to two chunks: 16 warps, warp 1 = TMEM owner + MMA
+// issuer, one epilogue warp per lane quarter (12..15). Four chunks: 17 warps, warps 0..3 a second
+// epilogue group (chunks 2, 3; 12..15 take chunks 0, 1) and warp 16 the MMA issuer -- one
+// epilogue warp walking four chunks is a latency chain that paces the whole pipeline.
+template <int NCH> struct TrShape {
+  static constexpr int kThreads = NCH > 2 ? 544 : 512;
+  static constexpr int kMmaWarp = NCH > 2 ? 16 : 1;
+  static constexpr int kEpiWarps = NCH > 2 ? 8 : 4;
+  static constexpr int kEpiChunks = NCH > 2 ? NCH / 2 : NCH;  // chunks per epilogue warp
+};
+
 template <int NCH, bool SPLIT>
-__global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs a) {
+__global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(const TrArgs a) {
+  using Shape = TrShape<NCH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int N = NCH * 32;
   // TMEM columns of one decoded tile (fp16 pairs): d, or 2d for [hi | lo] rows
@@ -128,7 +172,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     for (int s = 0; s < S; ++s) {
       mbar_init(afull_bar(s), 8);  // the two decoder warps of each lane quarter
       mbar_init(accf_bar(s), 1);
-      mbar_init(free_bar(s), 4);   // the four epilogue warps
+      mbar_init(free_bar(s), Shape::kEpiWarps);
     }
     mbar_init(done_bar, 1);
     misc->abort = (sbase & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
@@ -193,7 +237,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       const int qi = c / a.nchunk;
       const int rq = (c - qi * a.nchunk) * 32 + (n_row & 31);
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (rq < a.nq)
+      if (rq < a.nq && c < a.n_chunks)  // three chunks run on the four-chunk kernel: zero rows
         val = __ldg(reinterpret_cast<const uint4*>(a.Q + (static_cast<int64_t>(qi) * a.nq + rq) * a.d) + u);
       const uint32_t off = static_cast<uint32_t>((u >> 3) * N * 128 + n_row * 128) +
                            ((static_cast<uint32_t>(u & 7) ^ static_cast<uint32_t>(n_row & 7)) << 4);
@@ -201,7 +245,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
   }
-  if (warp == 1) {
+  if (warp == Shape::kMmaWarp) {
     tmem_alloc(smem_u32(&misc->tmem), 512);
     tmem_relinquish();
   }
@@ -218,7 +262,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
 
   if (*abort_flag) {
     // misaligned shared memory: no role runs (the error word says why)
-  } else if (warp == 1) {
+  } else if (warp == Shape::kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc(128, N, 0u);
@@ -310,11 +354,11 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       __syncwarp();
       if (lane == 0) mbar_arrive(afull_bar(s));
     }
-  } else if (warp >= kTrEpiWarp0) {
+  } else if (warp >= kTrEpiWarp0 || (NCH > 2 && warp < 4)) {
     // ------------------------------------------------------------------ epilogue
     // Lane l keeps, per query row i, the running max acc[c][i] over the tokens of the open
     // document that sit on lane l (token lo + 32 j + l of every window j). A document's row maxima
-    // need the max across lanes, taken once when the document ends (xpose_max32), not per window.
+    // need the max across lanes, taken once when the document ends (xpose_max), not per window.
     const int q = warp & 3;
     const int64_t lo = misc->sub_tok[q], hi = misc->sub_tok[q + 1];
     const int64_t dhi = misc->sub_doc[q + 1];
@@ -335,21 +379,31 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     auto emit = [&](int c, int64_t dd, float x) {
       const int rq = (c % a.nchunk) * 32 + lane;
       const float s = warp_sum(rq < a.nq ? x : 0.0f);
-      if (lane == 0) a.out[static_cast<int64_t>(c) * docs.n_docs + dd] = s;
+      if (lane == 0 && c < a.n_chunks) a.out[static_cast<int64_t>(c) * docs.n_docs + dd] = s;
     };
-    float acc[NCH][32];
-    bool touched[NCH];  // warp-uniform: acc[c] holds tokens of the open document
+    // this warp's chunks: cbase .. cbase + EC - 1
+    constexpr int EC = Shape::kEpiChunks;
+    const int cbase = (NCH > 2 && warp < 4) ? EC : 0;
+    // running maxima: 32 per chunk elementwise, or 16 folded once per window (four chunks: the
+    // 544-thread block leaves 120 registers a thread)
+    constexpr int W = NCH > 2 ? 16 : 32;
+    float acc[EC][W];
+    bool touched[EC];  // warp-uniform: acc[c] holds tokens of the open document
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
+    for (int c = 0; c < EC; ++c) {
       touched[c] = false;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
+      for (int i = 0; i < W; ++i) acc[c][i] = kTrNegInf;
     }
     auto finish = [&](int c, int64_t dd) {
-      const float x = touched[c] ? xpose_max32(acc[c]) : kTrNegInf;
-      emit(c, dd, x);
+      float x = kTrNegInf;
+      if (touched[c]) {
+        if constexpr (W == 16) x = xpose_max16(acc[c]);
+        else x = xpose_max32(acc[c]);
+      }
+      emit(cbase + c, dd, x);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
+      for (int i = 0; i < W; ++i) acc[c][i] = kTrNegInf;
       touched[c] = false;
     };
     int64_t doc = misc->sub_doc[q];
@@ -365,11 +419,11 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       const int nv = hi - tb >= 32 ? 32 : (hi > tb ? static_cast<int>(hi - tb) : 0);
       const int64_t doc0 = doc, dend0 = dend;
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
+      for (int c = 0; c < EC; ++c) {
         uint32_t r[32];
-        tmem_ld32_async(t_quarter + acc_col(s) + 32u * c, r);
+        tmem_ld32_async(t_quarter + acc_col(s) + 32u * (cbase + c), r);
         tmem_wait_ld32(r);
-        if (c == NCH - 1) {  // the slot's last read: hand it back before the math
+        if (c == EC - 1) {  // the slot's last read: hand it back before the math
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(free_bar(s));
@@ -385,7 +439,9 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
           }
           const int64_t e = dend - tb;
           const int p_hi = e < nv ? static_cast<int>(e) : nv;
-          if (p == 0 && p_hi == 32) {
+          if constexpr (W == 16) {
+            fold16(acc[c], r, lane >= p && lane < p_hi);
+          } else if (p == 0 && p_hi == 32) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc[c][i] = fmaxf(acc[c][i], __uint_as_float(r[i]));
           } else {
@@ -401,7 +457,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     if (ok) {
       // the document open at the end of the quarter, then any empty ones after it
 #pragma unroll
-      for (int c = 0; c < NCH; ++c) {
+      for (int c = 0; c < EC; ++c) {
         for (int64_t dd = doc; dd < dhi; ++dd) finish(c, dd);
       }
     }
@@ -409,7 +465,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == Shape::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
@@ -444,14 +500,16 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   const int64_t nchunk = (nq + 31) / 32;
   const int64_t chunks = n_queries * nchunk;
   const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
-  if (chunks < 1 || chunks > kTrMaxChunks || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
+  if (chunks < 1 || chunks > (split ? kTrMaxChunksSplit : kTrMaxChunks) || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
       K > 256 || cb_bytes > (split ? 128 : 96) * 1024 || n_tokens <= 0 ||
       (reinterpret_cast<uintptr_t>(Q) & 15))
     return TMS_ERR_UNSUPPORTED;
   int status = TMS_OK;
   const DeviceInfo* dev = current_device_info(&status);
   if (!dev) return status;
-  const int N = static_cast<int>(chunks) * 32;
+  // the kernel's query tile is NCH x 32 rows: three chunks run on the four-chunk kernel
+  const int nch = chunks > 2 ? 4 : static_cast<int>(chunks);
+  const int N = nch * 32;
   const int acols = static_cast<int>(d / 2) * (split ? 2 : 1);
   // as many slots as TMEM holds: a hand-off through an mbarrier takes ~500 cycles, so several
   // tiles must be in flight between the decoders, the MMA and the epilogue
@@ -495,12 +553,15 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   const size_t half = static_cast<size_t>(dev->max_smem_optin) / 2 + 1024;
   if (smem < half) smem = half;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
-  auto kern = split ? ((chunks == 1) ? pq_tokrows_kernel<1, true> : pq_tokrows_kernel<2, true>)
-                    : ((chunks == 1) ? pq_tokrows_kernel<1, false> : pq_tokrows_kernel<2, false>);
+  auto kern = split ? ((nch == 1)   ? pq_tokrows_kernel<1, true>
+                       : (nch == 2) ? pq_tokrows_kernel<2, true>
+                                    : pq_tokrows_kernel<4, true>)
+                    : ((nch == 1) ? pq_tokrows_kernel<1, false> : pq_tokrows_kernel<2, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return TMS_ERR_CUDA;
-  kern<<<static_cast<unsigned>(ranges), kTrThreads, smem, st>>>(a);
+  const int threads = nch > 2 ? TrShape<4>::kThreads : TrShape<1>::kThreads;
+  kern<<<static_cast<unsigned>(ranges), threads, smem, st>>>(a);
   if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
   if (nchunk == 1) return TMS_OK;
   const int64_t total = n_queries * n_docs;
