@@ -169,7 +169,8 @@ def test_full_size_rerank_consistency(cuda_device):
     close(sub, O.maxsim_ragged(Qb.cpu(), Dsub.cpu(), sub_off))
 
 
-@pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor", "pq_token_rows", "pq_precise"])
+@pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor", "pq_token_rows", "pq_precise",
+                                  "pq_precise4"])
 def test_bounded_wait_reports_timeout(case, cuda_device):
     """Fault knob: the producer issues no load, so every consumer wait runs out after the (short)
     limit; the kernel returns, the host reads TMS_ERR_TIMEOUT, and the context stays usable."""
@@ -177,11 +178,13 @@ def test_bounded_wait_reports_timeout(case, cuda_device):
     lib = _lib.load()
     if case.startswith("pq"):
         cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
-        pq = TileMaxSimPQ(cb, exact=(case == "pq_precise"))
+        pq = TileMaxSimPQ(cb, exact=case.startswith("pq_precise"))
         codes = torch.randint(0, 256, (40 * 64, 16), generator=R.gen(4), dtype=torch.uint8).to(cuda_device)
         off = (torch.arange(41, dtype=torch.int64) * 64).to(cuda_device)
-        # 5 queries: decoder-warp variant of the dense kernel; 1 query: token-rows kernel
-        Qb = R.normalized((5 if case == "pq_tensor" else 1, 32, 128), 5).to(cuda_device)
+        # 5 queries: decoder-warp variant of the dense kernel; 1 query: token-rows kernel; 4 queries
+        # at the default precision: the four-chunk token-rows kernel (MMAs issued by a decoder warp)
+        nqry = {"pq_tensor": 5, "pq_precise4": 4}.get(case, 1)
+        Qb = R.normalized((nqry, 32, 128), 5).to(cuda_device)
         run = lambda: pq.score_queries(Qb, codes, off)  # noqa: E731
         want = O.pq_maxsim_adc_ragged(Qb.cpu(), cb.cpu(), codes.cpu(), off.cpu().numpy())
         tol = (1e-3, 5e-3)

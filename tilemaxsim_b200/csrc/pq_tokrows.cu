@@ -31,8 +31,9 @@
 // Warp roles (one or two chunks, 512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 =
 // decoders (lane quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column
 // blocks of every tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only
-// help in the prologue. Three or four chunks (codebook split only; 544 threads): warps 0..3 are a
-// second epilogue group and warp 16 is the MMA issuer (TrShape).
+// help in the prologue. Three or four chunks (codebook split only): warps 0..3 are a second
+// epilogue group and warp 4, a decoder, also issues the MMAs (TrShape).
+#include <cuda/atomic>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -43,6 +44,7 @@ namespace tms {
 
 namespace {
 
+constexpr int kTrThreads = 512;
 constexpr int kTrDecWarp0 = 4;
 constexpr int kTrEpiWarp0 = 12;
 constexpr int kTrMaxChunks = 2;       // N = 32 x chunks <= 64 query rows per CTA
@@ -84,6 +86,7 @@ struct TrMisc {
   int n_tiles;
   int64_t sub_doc[5];
   int64_t sub_tok[5];
+  uint32_t arrivals[8];  // decoder warps done with the slot's tiles (the last one issues the MMAs)
 };
 
 // Lane l receives max over the 32 lanes of v[l]; destroys v. 31 shuffles: at each step a lane
@@ -103,48 +106,29 @@ __device__ __forceinline__ float xpose_max32(float (&v)[32]) {
   return v[0];
 }
 
-// The first transposing step of xpose_max32 applied to one window r and max-merged into the
-// 16-value state acc: the step's outputs are maxima of fixed inputs, so max commutes with it and
-// the state of many windows finishes with xpose_max16. Halves the registers a chunk's running
-// maxima take. Lanes with in == false contribute -inf (tokens of another document).
-__device__ __forceinline__ void fold16(float (&acc)[16], const uint32_t (&r)[32], bool in) {
-  const bool up = (threadIdx.x & 16) != 0;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float send = in ? __uint_as_float(up ? r[i] : r[i + 16]) : kTrNegInf;
-    const float keep = in ? __uint_as_float(up ? r[i + 16] : r[i]) : kTrNegInf;
-    acc[i] = fmaxf(acc[i], fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16)));
-  }
-}
-// The remaining 15 shuffles of xpose_max32 on a state folded by fold16.
-__device__ __forceinline__ float xpose_max16(float (&v)[16]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1) {
-    const bool up = (lane & w) != 0;
-#pragma unroll
-    for (int i = 0; i < w; ++i) {
-      const float send = up ? v[i] : v[i + w];
-      const float keep = up ? v[i + w] : v[i];
-      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
-    }
-  }
-  return v[0];
+// Block shape per query-chunk count (512 threads, 128 registers a thread). Up to two chunks:
+// warp 1 = TMEM owner + MMA issuer, one epilogue warp per lane quarter (12..15). Four chunks:
+// warps 0..3 are a second epilogue group (chunks 2, 3; 12..15 take chunks 0, 1) -- one epilogue
+// warp walking four chunks is a latency chain that paces the whole pipeline -- the first decoder
+// warp owns TMEM, and the last decoder warp to finish a tile issues its MMAs.
+// Last-arriver hand-off: a decoder warp's lane 0 counts its finished tile into the slot's counter
+// (acq_rel, after tcgen05.fence::before_thread_sync); the eighth arrival sees every decoder's
+// TMEM stores and issues the MMAs itself, so no thread waits for the slowest decoder.
+// The counter only grows (the k-th use of a slot counts 8k .. 8k + 7; wrap-around keeps that).
+__device__ __forceinline__ uint32_t count_arrival(uint32_t* ctr) {
+  cuda::atomic_ref<uint32_t, cuda::thread_scope_block> ref(*ctr);
+  return ref.fetch_add(1, cuda::memory_order_acq_rel);
 }
 
-// Block shape per query-chunk count. Up to two chunks: 16 warps, warp 1 = TMEM owner + MMA
-// issuer, one epilogue warp per lane quarter (12..15). Four chunks: 17 warps, warps 0..3 a second
-// epilogue group (chunks 2, 3; 12..15 take chunks 0, 1) and warp 16 the MMA issuer -- one
-// epilogue warp walking four chunks is a latency chain that paces the whole pipeline.
 template <int NCH> struct TrShape {
-  static constexpr int kThreads = NCH > 2 ? 544 : 512;
-  static constexpr int kMmaWarp = NCH > 2 ? 16 : 1;
+  static constexpr bool kMmaInDecoder = NCH > 2;
+  static constexpr int kTmemWarp = NCH > 2 ? kTrDecWarp0 : 1;
   static constexpr int kEpiWarps = NCH > 2 ? 8 : 4;
   static constexpr int kEpiChunks = NCH > 2 ? NCH / 2 : NCH;  // chunks per epilogue warp
 };
 
 template <int NCH, bool SPLIT>
-__global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(const TrArgs a) {
+__global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs a) {
   using Shape = TrShape<NCH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int N = NCH * 32;
@@ -174,7 +158,9 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
       mbar_init(accf_bar(s), 1);
       mbar_init(free_bar(s), Shape::kEpiWarps);
     }
-    mbar_init(done_bar, 1);
+    // the MMA-issuing threads commit to done_bar once each at the end
+    mbar_init(done_bar, Shape::kMmaInDecoder ? 8 : 1);
+    for (int i = 0; i < 8; ++i) misc->arrivals[i] = 0u;
     misc->abort = (sbase & 1023u) ? 1 : 0;  // SWIZZLE_128B needs a 1024-aligned base
     misc->never = 0;
     if (misc->abort) atomicCAS(a.err, 0u, kDevErrTimeout | 31u);
@@ -245,7 +231,7 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
   }
-  if (warp == Shape::kMmaWarp) {
+  if (warp == Shape::kTmemWarp) {
     tmem_alloc(smem_u32(&misc->tmem), 512);
     tmem_relinquish();
   }
@@ -260,28 +246,40 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
   auto a_col = [&](int s) { return static_cast<uint32_t>(s * acols); };
   auto acc_col = [&](int s) { return static_cast<uint32_t>(S * acols + s * N); };
 
-  if (*abort_flag) {
+  // One thread, once tile j's decoded rows are all in TMEM: S^T = tile . Q^T.
+  auto mma_tile = [&](int s) {
+    const uint32_t idesc = make_idesc(128, N, 0u);
+    // split codebook: K runs over [hi | lo] columns of A against the query rows twice
+    const int kd = a.d / 16;
+    for (int k = 0; k < acols / 8; ++k) {
+      const int kq = (SPLIT && k >= kd) ? k - kd : k;
+      const uint64_t bd = sw128_kmajor_desc(b_s + static_cast<uint32_t>((kq >> 2) * N * 128 + (kq & 3) * 32));
+      mma_f16_ts(tmem_base + acc_col(s), tmem_base + a_col(s) + 8u * k, bd, idesc, k != 0);
+    }
+    mma_commit(accf_bar(s));
+  };
+  auto issue_tile = [&](int j) -> bool {
+    const int s = j % S;
+    if (!mbar_wait(afull_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 21)) return false;
+    tc_fence_after();
+    mma_tile(s);
+    return true;
+  };
+  // every MMA the issuing thread launched lands before TMEM is released (bounded by time only)
+  auto drain_mma = [&]() {
+    mma_commit(done_bar);
+    mbar_wait(done_bar, 0, &misc->never, tmo, a.err, 22);
+  };
+
+  const bool roles_run = !*abort_flag;
+  if (!roles_run) {
     // misaligned shared memory: no role runs (the error word says why)
-  } else if (warp == Shape::kMmaWarp) {
+  } else if (!Shape::kMmaInDecoder && warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(128, N, 0u);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % S;
-        if (!mbar_wait(afull_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 21)) break;
-        tc_fence_after();
-        // split codebook: K runs over [hi | lo] columns of A against the query rows twice
-        const int kd = a.d / 16;
-        for (int k = 0; k < acols / 8; ++k) {
-          const int kq = (SPLIT && k >= kd) ? k - kd : k;
-          const uint64_t bd = sw128_kmajor_desc(b_s + static_cast<uint32_t>((kq >> 2) * N * 128 + (kq & 3) * 32));
-          mma_f16_ts(tmem_base + acc_col(s), tmem_base + a_col(s) + 8u * k, bd, idesc, k != 0);
-        }
-        mma_commit(accf_bar(s));
-      }
-      // every MMA this thread issued lands before TMEM is released (bounded by time only)
-      mma_commit(done_bar);
-      mbar_wait(done_bar, 0, &misc->never, tmo, a.err, 22);
+      for (int j = 0; j < n_tiles; ++j)
+        if (!issue_tile(j)) break;
+      drain_mma();
     }
   } else if (warp >= kTrDecWarp0 && warp < kTrEpiWarp0) {
     // ------------------------------------------------------------------ decoders
@@ -352,62 +350,69 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(afull_bar(s));
+      if (!Shape::kMmaInDecoder) {
+        if (lane == 0) mbar_arrive(afull_bar(s));
+      } else if (lane == 0 && (count_arrival(&misc->arrivals[s]) & 7u) == 7u) {
+        tc_fence_after();
+        mma_tile(s);
+      }
     }
-  } else if (warp >= kTrEpiWarp0 || (NCH > 2 && warp < 4)) {
+    // each decoder warp commits once: done_bar completes when every MMA it issued has landed
+    if (Shape::kMmaInDecoder && lane == 0) mma_commit(done_bar);
+  } else if (warp >= kTrEpiWarp0 || (Shape::kEpiWarps == 8 && warp < 4)) {
     // ------------------------------------------------------------------ epilogue
     // Lane l keeps, per query row i, the running max acc[c][i] over the tokens of the open
     // document that sit on lane l (token lo + 32 j + l of every window j). A document's row maxima
     // need the max across lanes, taken once when the document ends (xpose_max), not per window.
+    // Positions are 32-bit, relative to the quarter's first token and first document (the host
+    // admits corpora of fewer than 2^31 - 64 tokens and documents): registers are what limits
+    // the four-chunk epilogue.
     const int q = warp & 3;
-    const int64_t lo = misc->sub_tok[q], hi = misc->sub_tok[q + 1];
-    const int64_t dhi = misc->sub_doc[q + 1];
+    const int64_t lo = misc->sub_tok[q];
+    const int qlen = static_cast<int>(misc->sub_tok[q + 1] - lo);
+    const int64_t doc_first = misc->sub_doc[q];
+    const int ndq = static_cast<int>(misc->sub_doc[q + 1] - doc_first);
     const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    // document ends fetched 32 at a time and handed out with shuffles
-    int64_t e_base = INT64_MIN / 2, ends = 0;
-    auto doc_end = [&](int64_t dd) -> int64_t {
-      if (dd >= dhi) return INT64_MAX;
-      int64_t idx = dd - e_base;
+    // document ends (relative) fetched 32 at a time and handed out with shuffles
+    int e_base = INT_MIN / 2, ends = 0;
+    auto doc_end = [&](int dd) -> int {
+      if (dd >= ndq) return INT_MAX;
+      int idx = dd - e_base;
       if (idx < 0 || idx >= 32) {
         e_base = dd;
-        const int64_t jj = dd + 1 + lane;
-        ends = (jj <= docs.n_docs) ? docs.start(jj) : INT64_MAX;
+        const int64_t jj = doc_first + dd + 1 + lane;
+        int64_t e = (jj <= docs.n_docs) ? docs.start(jj) - lo : INT_MAX;
+        e = e > INT_MAX ? INT_MAX : (e < -(1LL << 30) ? -(1LL << 30) : e);  // malformed offsets
+        ends = static_cast<int>(e);
         idx = 0;
       }
-      return __shfl_sync(0xffffffffu, ends, static_cast<int>(idx));
+      return __shfl_sync(0xffffffffu, ends, idx);
     };
-    auto emit = [&](int c, int64_t dd, float x) {
+    auto emit = [&](int c, int dd, float x) {
       const int rq = (c % a.nchunk) * 32 + lane;
       const float s = warp_sum(rq < a.nq ? x : 0.0f);
-      if (lane == 0 && c < a.n_chunks) a.out[static_cast<int64_t>(c) * docs.n_docs + dd] = s;
+      if (lane == 0 && c < a.n_chunks) a.out[static_cast<int64_t>(c) * docs.n_docs + doc_first + dd] = s;
     };
     // this warp's chunks: cbase .. cbase + EC - 1
     constexpr int EC = Shape::kEpiChunks;
     const int cbase = (NCH > 2 && warp < 4) ? EC : 0;
-    // running maxima: 32 per chunk elementwise, or 16 folded once per window (four chunks: the
-    // 544-thread block leaves 120 registers a thread)
-    constexpr int W = NCH > 2 ? 16 : 32;
-    float acc[EC][W];
+    float acc[EC][32];
     bool touched[EC];  // warp-uniform: acc[c] holds tokens of the open document
 #pragma unroll
     for (int c = 0; c < EC; ++c) {
       touched[c] = false;
 #pragma unroll
-      for (int i = 0; i < W; ++i) acc[c][i] = kTrNegInf;
+      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
     }
-    auto finish = [&](int c, int64_t dd) {
-      float x = kTrNegInf;
-      if (touched[c]) {
-        if constexpr (W == 16) x = xpose_max16(acc[c]);
-        else x = xpose_max32(acc[c]);
-      }
+    auto finish = [&](int c, int dd) {
+      const float x = touched[c] ? xpose_max32(acc[c]) : kTrNegInf;
       emit(cbase + c, dd, x);
 #pragma unroll
-      for (int i = 0; i < W; ++i) acc[c][i] = kTrNegInf;
+      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
       touched[c] = false;
     };
-    int64_t doc = misc->sub_doc[q];
-    int64_t dend = doc_end(doc);
+    int doc = 0;
+    int dend = doc_end(doc);
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j % S;
@@ -415,9 +420,9 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
       if (lane == 0) w = mbar_wait(accf_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 24);
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
       tc_fence_after();
-      const int64_t tb = lo + 32LL * j;
-      const int nv = hi - tb >= 32 ? 32 : (hi > tb ? static_cast<int>(hi - tb) : 0);
-      const int64_t doc0 = doc, dend0 = dend;
+      const int tb = 32 * j;
+      const int nv = qlen - tb >= 32 ? 32 : (qlen > tb ? qlen - tb : 0);
+      const int doc0 = doc, dend0 = dend;
 #pragma unroll
       for (int c = 0; c < EC; ++c) {
         uint32_t r[32];
@@ -437,11 +442,9 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
             ++doc;
             dend = doc_end(doc);
           }
-          const int64_t e = dend - tb;
-          const int p_hi = e < nv ? static_cast<int>(e) : nv;
-          if constexpr (W == 16) {
-            fold16(acc[c], r, lane >= p && lane < p_hi);
-          } else if (p == 0 && p_hi == 32) {
+          const int e = dend - tb;
+          const int p_hi = e < nv ? e : nv;
+          if (p == 0 && p_hi == 32) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc[c][i] = fmaxf(acc[c][i], __uint_as_float(r[i]));
           } else {
@@ -458,14 +461,17 @@ __global__ void __launch_bounds__(TrShape<NCH>::kThreads, 1) pq_tokrows_kernel(c
       // the document open at the end of the quarter, then any empty ones after it
 #pragma unroll
       for (int c = 0; c < EC; ++c) {
-        for (int64_t dd = doc; dd < dhi; ++dd) finish(c, dd);
+        for (int dd = doc; dd < ndq; ++dd) finish(c, dd);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == Shape::kMmaWarp) {
+  if (warp == Shape::kTmemWarp) {
+    // decoder-issued MMAs: all eight commits are in (before the barrier); wait for the MMAs
+    if (Shape::kMmaInDecoder && roles_run && lane == 0) mbar_wait(done_bar, 0, &misc->never, tmo, a.err, 22);
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
@@ -500,7 +506,10 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   const int64_t nchunk = (nq + 31) / 32;
   const int64_t chunks = n_queries * nchunk;
   const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
-  if (chunks < 1 || chunks > (split ? kTrMaxChunksSplit : kTrMaxChunks) || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
+  // the epilogue walks 32-bit positions (token and document indices)
+  constexpr int64_t kMax32 = 0x7fffffffLL - 64;
+  if (chunks < 1 || chunks > (split ? kTrMaxChunksSplit : kTrMaxChunks) || n_tokens > kMax32 ||
+      n_docs > kMax32 || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
       K > 256 || cb_bytes > (split ? 128 : 96) * 1024 || n_tokens <= 0 ||
       (reinterpret_cast<uintptr_t>(Q) & 15))
     return TMS_ERR_UNSUPPORTED;
@@ -560,8 +569,7 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return TMS_ERR_CUDA;
-  const int threads = nch > 2 ? TrShape<4>::kThreads : TrShape<1>::kThreads;
-  kern<<<static_cast<unsigned>(ranges), threads, smem, st>>>(a);
+  kern<<<static_cast<unsigned>(ranges), kTrThreads, smem, st>>>(a);
   if (cudaGetLastError() != cudaSuccess) return TMS_ERR_CUDA;
   if (nchunk == 1) return TMS_OK;
   const int64_t total = n_queries * n_docs;
