@@ -309,27 +309,43 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       int w = 0;
       if (lane == 0) w = mbar_wait(free_bar(s), ((j / S) & 1u) ^ 1u, abort_flag, tmo, a.err, 23);
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
-      const int64_t tok = lo + 32LL * j + lane;
-      const bool valid = tok < hi;
       const int hblocks = a.d / 64;
-      for (int h = hp; h < hblocks * (SPLIT ? 2 : 1); h += 2) {
-        // block h of the decoded row: column block hh of the hi table, or of the lo table
-        const bool lo_half = SPLIT && h >= hblocks;
-        const int hh = lo_half ? h - hblocks : h;
-        const __half* tab = lo_half ? cbs + n_cb : cbs;
-        uint32_t r[32];
-        if (fast) {  // h == hp: subspaces 8 hp .. 8 hp + 7
+      if (fast) {
+        // d = 128: this warp's block h = hp holds subspaces 8 hp .. 8 hp + 7. Lanes past the
+        // quarter's last token decode code 0 (load_codes) and the epilogue never reads them.
+        // Split codebook: the lo row sits at a fixed offset from the hi row, so one code and one
+        // address serve both loads, and the lo values go to block hp + hblocks.
+        const char* tab = reinterpret_cast<const char*>(cbs);
+        uint32_t off[8];  // byte offsets of the 8 codebook rows in the hi table
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t code = ((i < 4 ? cc.x : cc.y) >> (8 * (i & 3))) & 0xffu;
+          code = min(code, kmax);  // never read past the codebook
+          off[i] = (static_cast<uint32_t>((8 * hp + i) * a.K) + code) * 16u;
+        }
+#pragma unroll
+        for (int half = 0; half < (SPLIT ? 2 : 1); ++half) {
+          const char* t = tab + (half ? n_cb * 2 : 0);
+          uint32_t r[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            uint32_t code = ((i < 4 ? cc.x : cc.y) >> (8 * (i & 3))) & 0xffu;
-            code = min(code, kmax);  // never read past the codebook
-            const uint4 e = *reinterpret_cast<const uint4*>(tab + ((8 * hp + i) * a.K + code) * 8);
-            r[4 * i] = valid ? e.x : 0u;
-            r[4 * i + 1] = valid ? e.y : 0u;
-            r[4 * i + 2] = valid ? e.z : 0u;
-            r[4 * i + 3] = valid ? e.w : 0u;
+            const uint4 e = *reinterpret_cast<const uint4*>(t + off[i]);
+            r[4 * i] = e.x;
+            r[4 * i + 1] = e.y;
+            r[4 * i + 2] = e.z;
+            r[4 * i + 3] = e.w;
           }
-        } else {
+          tmem_st32(t_quarter + a_col(s) + 32u * (hp + half * hblocks), r);
+        }
+      } else {
+        const int64_t tok = lo + 32LL * j + lane;
+        const bool valid = tok < hi;
+        for (int h = hp; h < hblocks * (SPLIT ? 2 : 1); h += 2) {
+          // block h of the decoded row: column block hh of the hi table, or of the lo table
+          const bool lo_half = SPLIT && h >= hblocks;
+          const int hh = lo_half ? h - hblocks : h;
+          const __half* tab = lo_half ? cbs + n_cb : cbs;
+          uint32_t r[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int col = 8 * (8 * hh + i);  // first element of this 16-byte unit
@@ -344,8 +360,8 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
             r[4 * i + 2] = e.z;
             r[4 * i + 3] = e.w;
           }
+          tmem_st32(t_quarter + a_col(s) + 32u * h, r);
         }
-        tmem_st32(t_quarter + a_col(s) + 32u * h, r);
       }
       tmem_wait_st();
       tc_fence_before();
