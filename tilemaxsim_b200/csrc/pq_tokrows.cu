@@ -19,12 +19,14 @@
 //    swizzle K-major layout. S^T = Dtile . Q^T lands with one token per TMEM lane and one query row
 //    per column.
 //  * The CTA's token range (cut at document boundaries) is cut again into four document-aligned
-//    sub-ranges, one per TMEM lane quarter: lane 32q + l of tile j holds token sub_tok[q] + 32j + l.
-//    Every epilogue warp therefore walks one contiguous token stream and owns whole documents:
-//    no cross-warp merge, deterministic results.
-//  * Epilogue: lane l keeps the running max over its tokens of the open document for every query
-//    row (elementwise, no shuffles); when the document ends, a transposing max (31 shuffles)
-//    leaves row l's maximum in lane l and a warp sum over the query rows gives the score.
+//    sub-ranges, one per TMEM lane quarter, and each lane of a quarter walks its own documents:
+//    lane l takes the quarter's documents l, l + 32, l + 64, ..., one token per tile, so TMEM lane
+//    32q + l of tile j holds the j-th token of lane l's document stream (LaneDocs). A document
+//    therefore lives on one lane: no cross-lane reduction, deterministic results.
+//  * Epilogue: lane l keeps the running max over its document's tokens for every query row
+//    (elementwise, registers); when the document ends, the lane sums its row maxima and stores
+//    the score -- no shuffles (they share the shared-memory pipe that the decoders' codebook
+//    gathers fill) and no walk over document boundaries inside a tile.
 //  * A hand-off through an mbarrier costs ~500 cycles on this part, so TMEM holds as many tiles
 //    in flight as fit (5 at N = 32: 64 decoded-token columns + 32 accumulator columns each).
 //
@@ -85,32 +87,69 @@ struct TrMisc {
   int never;  // stays 0: the final drain wait is bounded by time only
   int n_tiles;
   int64_t sub_doc[5];
-  int64_t sub_tok[5];
   uint32_t arrivals[8];  // decoder warps done with the slot's tiles (the last one issues the MMAs)
 };
 
-// Lane l receives max over the 32 lanes of v[l]; destroys v. 31 shuffles: at each step a lane
-// keeps the half of its values whose row index has its own lane bit and trades the other half.
-__device__ __forceinline__ float xpose_max32(float (&v)[32]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool up = (lane & w) != 0;
-#pragma unroll
-    for (int i = 0; i < w; ++i) {
-      const float send = up ? v[i] : v[i + w];
-      const float keep = up ? v[i + w] : v[i];
-      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
+template <bool kPos>  // kPos: track token positions (decoders); the epilogue needs counts only
+struct LaneDocs {
+  int64_t first;  // the quarter's first document (absolute)
+  int ndq;        // documents in the quarter
+  int d;          // current document (relative); >= ndq once the lane is done
+  int rem;        // tokens of d not yet handed out (> 0 while the lane is active)
+  int n_len;      // length of document d + 32, fetched one document ahead
+  int64_t pos;    // absolute index of the lane's next token (kPos)
+  int64_t n_start;  // start of document d + 32 (kPos)
+
+  __device__ __forceinline__ bool active() const { return d < ndq; }
+  // length (clamped to [0, 2^31)) and start of relative document dd; (0, 0) past the quarter
+  __device__ __forceinline__ int fetch(const DocLayout& docs, int dd, int64_t& st) const {
+    st = 0;
+    if (dd >= ndq) return 0;
+    st = docs.start(first + dd);
+    const int64_t e = docs.start(first + dd + 1) - st;
+    return e < 0 ? 0 : (e > 0x7fffffffLL ? 0x7fffffff : static_cast<int>(e));
+  }
+  __device__ __forceinline__ void advance(const DocLayout& docs) {
+    d += 32;
+    rem = n_len;
+    int64_t st;
+    if (kPos) pos = n_start;
+    n_len = fetch(docs, d + 32, st);
+    if (kPos) n_start = st;
+  }
+  // Move to the next non-empty document; on_empty(dd) for every empty one passed over.
+  template <class F>
+  __device__ __forceinline__ void next(const DocLayout& docs, F&& on_empty) {
+    advance(docs);
+    while (rem == 0 && d < ndq) {
+      on_empty(d);
+      advance(docs);
     }
   }
-  return v[0];
-}
+  template <class F>
+  __device__ __forceinline__ void init(const DocLayout& docs, int64_t first_, int ndq_, int lane, F&& on_empty) {
+    first = first_;
+    ndq = ndq_;
+    d = lane - 32;
+    int64_t st;
+    n_len = fetch(docs, lane, st);
+    n_start = st;
+    pos = 0;
+    next(docs, on_empty);
+  }
+  // After the lane's token of a tile: on_done(d) when that was the document's last token.
+  template <class G, class F>
+  __device__ __forceinline__ void step(const DocLayout& docs, G&& on_done, F&& on_empty) {
+    if (d < ndq) {
+      if (kPos) ++pos;
+      if (--rem == 0) {
+        on_done(d);
+        next(docs, on_empty);
+      }
+    }
+  }
+};
 
-// Block shape per query-chunk count (512 threads, 128 registers a thread). Up to two chunks:
-// warp 1 = TMEM owner + MMA issuer, one epilogue warp per lane quarter (12..15). Four chunks:
-// warps 0..3 are a second epilogue group (chunks 2, 3; 12..15 take chunks 0, 1) -- one epilogue
-// warp walking four chunks is a latency chain that paces the whole pipeline -- the first decoder
-// warp owns TMEM, and the last decoder warp to finish a tile issues its MMAs.
 // Last-arriver hand-off: a decoder warp's lane 0 counts its finished tile into the slot's counter
 // (acq_rel, after tcgen05.fence::before_thread_sync); the eighth arrival sees every decoder's
 // TMEM stores and issues the MMAs itself, so no thread waits for the slowest decoder.
@@ -186,21 +225,8 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       sd[q] = x > doc_hi ? doc_hi : x;
     }
     if (lane == 0) {
-      int64_t tiles = 0;
-      int64_t prev = 0;
-      for (int q = 0; q <= 4; ++q) {
-        misc->sub_doc[q] = sd[q];
-        // clamped (and kept non-decreasing) so malformed offsets never read outside `codes`
-        int64_t t = docs.start(sd[q]);
-        t = t < prev ? prev : (t > a.n_tokens ? a.n_tokens : t);
-        misc->sub_tok[q] = t;
-        prev = t;
-      }
-      for (int q = 0; q < 4; ++q) {
-        const int64_t t = (misc->sub_tok[q + 1] - misc->sub_tok[q] + 31) / 32;
-        tiles = t > tiles ? t : tiles;
-      }
-      misc->n_tiles = static_cast<int>(tiles);
+      for (int q = 0; q <= 4; ++q) misc->sub_doc[q] = sd[q];
+      misc->n_tiles = 0;
     }
   }
   // Stage the codebook as fp16 and the query rows as the swizzled B operand (every thread helps).
@@ -230,6 +256,24 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       *reinterpret_cast<uint4*>(smem + L.b_off + off) = val;
     }
     fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+  }
+  __syncthreads();
+  if (warp < 4) {
+    // tiles = the longest lane stream: the sum of the lengths of lane l's documents
+    const int64_t first = misc->sub_doc[warp];
+    const int ndq = static_cast<int>(misc->sub_doc[warp + 1] - first);
+    LaneDocs<false> ld;
+    ld.first = first;
+    ld.ndq = ndq;
+    uint32_t t = 0;
+#pragma unroll 4
+    for (int dd = lane; dd < ndq; dd += 32) {
+      int64_t st;
+      t += static_cast<uint32_t>(ld.fetch(docs, dd, st));
+      t = t > (1u << 30) ? (1u << 30) : t;  // malformed offsets: bounded, never read past `codes`
+    }
+    t = __reduce_max_sync(0xffffffffu, t);
+    if (lane == 0) atomicMax(&misc->n_tiles, static_cast<int>(t));
   }
   if (warp == Shape::kTmemWarp) {
     tmem_alloc(smem_u32(&misc->tmem), 512);
@@ -284,35 +328,43 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
   } else if (warp >= kTrDecWarp0 && warp < kTrEpiWarp0) {
     // ------------------------------------------------------------------ decoders
     // Warp (q, hp) rebuilds, for every tile, the 64-element column blocks h = hp, hp + 2, ... of
-    // the 32 token rows of lane quarter q (one tcgen05.st of 32 lanes x 32 columns per block).
+    // the 32 token rows of lane quarter q (one tcgen05.st of 32 lanes x 32 columns per block);
+    // lane l's row is the next token of its document stream.
     const int q = warp & 3;
     const int hp = (warp - kTrDecWarp0) >> 2;
-    const int64_t lo = misc->sub_tok[q], hi = misc->sub_tok[q + 1];
     const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     // d = 128, M = 16, dsub = 8: warp hp needs code bytes [8 hp, 8 hp + 8) of each token
     const bool fast = (a.M == 16) && (a.dsub == 8) && ((reinterpret_cast<uintptr_t>(a.codes) & 15) == 0);
     const uint32_t kmax = static_cast<uint32_t>(a.K - 1);
-    auto load_codes = [&](int j) -> uint2 {
-      const int64_t tok = lo + 32LL * j + lane;
-      return (fast && j < n_tiles && tok < hi)
-                 ? __ldg(reinterpret_cast<const uint2*>(a.codes + tok * 16 + 8 * hp))
-                 : make_uint2(0, 0);
+    auto nothing = [](int) {};
+    // The stream runs two tiles ahead of the decode in the fast case (codes of the next two
+    // tiles in flight), level with it otherwise (codes read inside the decode).
+    LaneDocs<true> ls;
+    ls.init(docs, misc->sub_doc[q], static_cast<int>(misc->sub_doc[q + 1] - misc->sub_doc[q]), lane, nothing);
+    auto load_codes = [&]() -> uint2 {
+      const bool in = ls.active() && ls.pos >= 0 && ls.pos < a.n_tokens;
+      const uint2 c = in ? __ldg(reinterpret_cast<const uint2*>(a.codes + ls.pos * 16 + 8 * hp)) : make_uint2(0, 0);
+      ls.step(docs, nothing, nothing);
+      return c;
     };
-    // codes of the next two tiles are in flight while this one is decoded
-    uint2 c_n1 = load_codes(0), c_n2 = load_codes(1);
+    uint2 c_n1 = make_uint2(0, 0), c_n2 = make_uint2(0, 0);
+    if (fast) {
+      c_n1 = load_codes();
+      c_n2 = load_codes();
+    }
     bool ok = !(a.debug_flags & 1);
     for (int j = 0; ok && j < n_tiles; ++j) {
       const uint2 cc = c_n1;
       c_n1 = c_n2;
-      c_n2 = load_codes(j + 2);
+      if (fast) c_n2 = load_codes();
       const int s = j % S;
       int w = 0;
       if (lane == 0) w = mbar_wait(free_bar(s), ((j / S) & 1u) ^ 1u, abort_flag, tmo, a.err, 23);
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
       const int hblocks = a.d / 64;
       if (fast) {
-        // d = 128: this warp's block h = hp holds subspaces 8 hp .. 8 hp + 7. Lanes past the
-        // quarter's last token decode code 0 (load_codes) and the epilogue never reads them.
+        // d = 128: this warp's block h = hp holds subspaces 8 hp .. 8 hp + 7. Lanes whose stream
+        // has ended decode code 0 (load_codes) and the epilogue never reads them.
         // Split codebook: the lo row sits at a fixed offset from the hi row, so one code and one
         // address serve both loads, and the lo values go to block hp + hblocks.
         const char* tab = reinterpret_cast<const char*>(cbs);
@@ -338,8 +390,8 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
           tmem_st32(t_quarter + a_col(s) + 32u * (hp + half * hblocks), r);
         }
       } else {
-        const int64_t tok = lo + 32LL * j + lane;
-        const bool valid = tok < hi;
+        const int64_t tok = ls.pos;
+        const bool valid = ls.active() && tok >= 0 && tok < a.n_tokens;
         for (int h = hp; h < hblocks * (SPLIT ? 2 : 1); h += 2) {
           // block h of the decoded row: column block hh of the hi table, or of the lo table
           const bool lo_half = SPLIT && h >= hblocks;
@@ -362,6 +414,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
           }
           tmem_st32(t_quarter + a_col(s) + 32u * h, r);
         }
+        ls.step(docs, nothing, nothing);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -377,58 +430,33 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     if (Shape::kMmaInDecoder && lane == 0) mma_commit(done_bar);
   } else if (warp >= kTrEpiWarp0 || (Shape::kEpiWarps == 8 && warp < 4)) {
     // ------------------------------------------------------------------ epilogue
-    // Lane l keeps, per query row i, the running max acc[c][i] over the tokens of the open
-    // document that sit on lane l (token lo + 32 j + l of every window j). A document's row maxima
-    // need the max across lanes, taken once when the document ends (xpose_max), not per window.
-    // Positions are 32-bit, relative to the quarter's first token and first document (the host
-    // admits corpora of fewer than 2^31 - 64 tokens and documents): registers are what limits
-    // the four-chunk epilogue.
+    // Lane l keeps, per query row i, the running max acc[c][i] over the tokens of its current
+    // document (one per tile); when the document's last token has been merged it sums the rows
+    // (in order i = 0, 1, ...) and stores the score. Empty documents score -inf.
     const int q = warp & 3;
-    const int64_t lo = misc->sub_tok[q];
-    const int qlen = static_cast<int>(misc->sub_tok[q + 1] - lo);
-    const int64_t doc_first = misc->sub_doc[q];
-    const int ndq = static_cast<int>(misc->sub_doc[q + 1] - doc_first);
     const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    // document ends (relative) fetched 32 at a time and handed out with shuffles
-    int e_base = INT_MIN / 2, ends = 0;
-    auto doc_end = [&](int dd) -> int {
-      if (dd >= ndq) return INT_MAX;
-      int idx = dd - e_base;
-      if (idx < 0 || idx >= 32) {
-        e_base = dd;
-        const int64_t jj = doc_first + dd + 1 + lane;
-        int64_t e = (jj <= docs.n_docs) ? docs.start(jj) - lo : INT_MAX;
-        e = e > INT_MAX ? INT_MAX : (e < -(1LL << 30) ? -(1LL << 30) : e);  // malformed offsets
-        ends = static_cast<int>(e);
-        idx = 0;
-      }
-      return __shfl_sync(0xffffffffu, ends, idx);
-    };
-    auto emit = [&](int c, int dd, float x) {
-      const int rq = (c % a.nchunk) * 32 + lane;
-      const float s = warp_sum(rq < a.nq ? x : 0.0f);
-      if (lane == 0 && c < a.n_chunks) a.out[static_cast<int64_t>(c) * docs.n_docs + doc_first + dd] = s;
-    };
     // this warp's chunks: cbase .. cbase + EC - 1
     constexpr int EC = Shape::kEpiChunks;
     const int cbase = (NCH > 2 && warp < 4) ? EC : 0;
+    // Padded query rows are zero, so their row maximum over a non-empty document is exactly 0 and
+    // the score sums all 32 rows of a chunk; every stored chunk has a real row, so an empty
+    // document scores -inf.
     float acc[EC][32];
-    bool touched[EC];  // warp-uniform: acc[c] holds tokens of the open document
 #pragma unroll
-    for (int c = 0; c < EC; ++c) {
-      touched[c] = false;
+    for (int c = 0; c < EC; ++c)
 #pragma unroll
       for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
-    }
-    auto finish = [&](int c, int dd) {
-      const float x = touched[c] ? xpose_max32(acc[c]) : kTrNegInf;
-      emit(cbase + c, dd, x);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c][i] = kTrNegInf;
-      touched[c] = false;
+    auto store = [&](int c, int dd, float x) {
+      if (cbase + c < a.n_chunks)
+        a.out[static_cast<int64_t>(cbase + c) * docs.n_docs + misc->sub_doc[q] + dd] = x;
     };
-    int doc = 0;
-    int dend = doc_end(doc);
+    auto on_empty = [&](int dd) {
+#pragma unroll
+      for (int c = 0; c < EC; ++c) store(c, dd, kTrNegInf);
+    };
+    auto nothing = [](int) {};
+    LaneDocs<false> ls;
+    ls.init(docs, misc->sub_doc[q], static_cast<int>(misc->sub_doc[q + 1] - misc->sub_doc[q]), lane, on_empty);
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j % S;
@@ -436,9 +464,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       if (lane == 0) w = mbar_wait(accf_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 24);
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
       tc_fence_after();
-      const int tb = 32 * j;
-      const int nv = qlen - tb >= 32 ? 32 : (qlen > tb ? qlen - tb : 0);
-      const int doc0 = doc, dend0 = dend;
+      const bool act = ls.active();
 #pragma unroll
       for (int c = 0; c < EC; ++c) {
         uint32_t r[32];
@@ -449,36 +475,25 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
           __syncwarp();
           if (lane == 0) mbar_arrive(free_bar(s));
         }
-        // the document walk is the same for every chunk: replay it from the window's start
-        doc = doc0;
-        dend = dend0;
-        for (int p = 0; p < nv;) {
-          while (dend <= tb + p) {  // documents that end before this position (empty ones too)
-            finish(c, doc);
-            ++doc;
-            dend = doc_end(doc);
-          }
-          const int e = dend - tb;
-          const int p_hi = e < nv ? e : nv;
-          if (p == 0 && p_hi == 32) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c][i] = fmaxf(acc[c][i], __uint_as_float(r[i]));
-          } else {
-            const bool in = lane >= p && lane < p_hi;
+        for (int i = 0; i < 32; ++i) acc[c][i] = act ? fmaxf(acc[c][i], __uint_as_float(r[i])) : acc[c][i];
+      }
+      // a document ends on this lane: its scores (summed by the whole warp, a uniform branch, so
+      // that no divergent region holds the accumulators), then the stream moves on
+      const bool ends = act && ls.rem == 1;
+      if (__any_sync(0xffffffffu, ends)) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c][i] = in ? fmaxf(acc[c][i], __uint_as_float(r[i])) : acc[c][i];
-          }
-          touched[c] = true;
-          p = p_hi;
+        for (int c = 0; c < EC; ++c) {
+          float x = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x += acc[c][i];
+          if (ends) store(c, ls.d, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c][i] = ends ? kTrNegInf : acc[c][i];
         }
       }
-    }
-    if (ok) {
-      // the document open at the end of the quarter, then any empty ones after it
-#pragma unroll
-      for (int c = 0; c < EC; ++c) {
-        for (int dd = doc; dd < ndq; ++dd) finish(c, dd);
-      }
+      ls.step(docs, nothing, on_empty);
+      __syncwarp();
     }
   }
 
