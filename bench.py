@@ -357,7 +357,7 @@ PQ_CONFIGS.update({f"{k}_fast": v for k, v in list(PQ_CONFIGS.items())})
 
 def pq_route(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> str:
     """The kernel tms_pq_maxsim picks for fp16 queries (csrc/pq_adc.cu routing): "tokrows" (the
-    token-rows tensor kernel) for 1-2 chunks of 32 query rows in fast mode, and at the default
+    token-rows tensor kernel) for 1-4 chunks of 32 query rows in fast mode, and at the default
     precision (codebook split into hi + lo) in passes of up to four chunks for queries of up to 128
     rows -- except batches of <= 8-token queries that need several passes; else "lut" (table
     lookups) at the default precision or "decoder" (the dense kernel's decoder warps) in fast
@@ -367,7 +367,7 @@ def pq_route(nqry: int, nq: int, M: int, K: int, dsub: int, exact: bool) -> str:
     d = M * dsub
     cb = M * K * dsub * 2 * (2 if exact else 1)
     shape_ok = d % 64 == 0 and d <= 256 and dsub % 8 == 0 and K <= 256 and cb <= (128 if exact else 96) * 1024
-    if shape_ok and (chunks <= 2 or (exact and nchunk <= 4 and (chunks <= 4 or nq >= 9))):
+    if shape_ok and (chunks <= 4 or (exact and nchunk <= 4 and nq >= 9)):
         return "tokrows"  # at the default precision: in passes of up to four chunks
     return "lut" if exact else "decoder"
 

@@ -102,12 +102,13 @@ def test_pq_ragged_multiquery(M, K, dsub, nq, path, cuda_device):
     (3, 16, 256, 8, 20, "ragged"), (1, 16, 256, 8, 64, "ragged"), (2, 32, 256, 8, 40, "ragged"),
     (1, 32, 256, 8, 32, "ragged"), (1, 8, 256, 8, 32, "ragged"), (2, 8, 256, 8, 30, "tiny"),
     (1, 8, 256, 16, 32, "ragged"), (1, 16, 100, 8, 5, "ragged"), (1, 16, 256, 8, 32, "tiny"),
-    (2, 16, 256, 8, 32, "one_long")])
+    (2, 16, 256, 8, 32, "one_long"), (4, 16, 256, 8, 32, "tiny"), (3, 16, 256, 8, 32, "one_long"),
+    (1, 16, 256, 8, 128, "ragged"), (5, 16, 256, 8, 32, "ragged")])
 def test_pq_small_batch_token_rows(nqry, M, K, dsub, nq, lengths, cuda_device):
-    """Small query batches (1-2 chunks of 32 query rows) take the token-rows tensor kernel: decoded
-    tokens in TMEM as the MMA's A operand, per-lane running maxima, a transposing max per finished
-    document (3-4 chunks check the decoder-warp kernel on the same cases). Ragged
-    corpora with empty documents, documents of 1-3 tokens (several boundaries per window), and one
+    """Small query batches (1-4 chunks of 32 query rows) take the token-rows tensor kernel: decoded
+    tokens in TMEM as the MMA's A operand, one document stream per TMEM lane, per-lane running
+    maxima summed when the lane's document ends (5 queries check the decoder-warp kernel). Ragged
+    corpora with empty documents, documents of 1-3 tokens (several documents per lane), and one
     document longer than a CTA's share of the corpus."""
     from tilemaxsim_b200 import TileMaxSimPQ
     if lengths == "ragged":

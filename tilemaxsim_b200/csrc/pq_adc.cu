@@ -468,7 +468,8 @@ extern "C" int tms_pq_maxsim(const void* Q, int q_dtype, int64_t n_queries, int6
   // Tensor-core path: codes decoded through a shared-memory fp16 codebook into MMA operand tiles
   // (fp16 queries, TMS_PQ_FAST); otherwise the exact fp32 table-lookup kernel below.
   if (mode == TMS_PQ_FAST && q_dtype == TMS_F16 && pq_mma_codebook_bytes(M, K, dsub)) {
-    // up to two 32-row query chunks: decoded tokens as the TMEM A operand (pq_tokrows.cu)
+    // up to four 32-row query chunks: decoded tokens as the TMEM A operand (pq_tokrows.cu); more
+    // chunks go to the dense kernel's decoder warps (one decode for the whole batch)
     {
       const int rc = pq_tokrows_maxsim(Q, n_queries, nq, codebook, cb_dtype, M, K, dsub, codes,
                                        n_tokens, doc_offsets, n_docs, nd_uniform, out, workspace,

@@ -1,6 +1,5 @@
-// pq_tokrows.cu -- PQ-ADC on the sm_100a tensor cores for small query batches (one or two
-// 32-row query chunks; up to four with the split codebook), with the document tokens on the TMEM
-// lanes.
+// pq_tokrows.cu -- PQ-ADC on the sm_100a tensor cores for small query batches (up to four
+// 32-row query chunks), with the document tokens on the TMEM lanes.
 //
 //   score[q, doc] = sum_i max_{j in doc} sum_m <Q[q,i,m*dsub:(m+1)*dsub], C[m, codes[j,m], :]>
 //
@@ -15,7 +14,7 @@
 //    straight into TMEM with tcgen05.st (lane = token, 32-bit column c = fp16 elements 2c, 2c+1).
 //    No shared-memory store and no replicated query tile: the only shared-memory traffic per token
 //    is the codebook gather (M random 16-byte reads at dsub = 8), which bounds the kernel.
-//  * The query rows are the B operand (N = 32 or 64), resident in shared memory in the 128-byte-
+//  * The query rows are the B operand (N = 32, 64 or 128), resident in shared memory in the 128-byte-
 //    swizzle K-major layout. S^T = Dtile . Q^T lands with one token per TMEM lane and one query row
 //    per column.
 //  * The CTA's token range (cut at document boundaries) is cut again into four document-aligned
@@ -33,7 +32,7 @@
 // Warp roles (one or two chunks, 512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 =
 // decoders (lane quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column
 // blocks of every tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only
-// help in the prologue. Three or four chunks (codebook split only): warps 0..3 are a second
+// help in the prologue. Three or four chunks: warps 0..3 are a second
 // epilogue group and warp 4, a decoder, also issues the MMAs (TrShape).
 #include <cuda/atomic>
 #include <cuda_bf16.h>
@@ -49,8 +48,7 @@ namespace {
 constexpr int kTrThreads = 512;
 constexpr int kTrDecWarp0 = 4;
 constexpr int kTrEpiWarp0 = 12;
-constexpr int kTrMaxChunks = 2;       // N = 32 x chunks <= 64 query rows per CTA
-constexpr int kTrMaxChunksSplit = 4;  // hi/lo rows: 128 query rows (two TMEM slots of 128 + 128)
+constexpr int kTrMaxChunks = 4;  // N = 32 x chunks <= 128 query rows per CTA (3 run as 4)
 constexpr float kTrNegInf = -__builtin_huge_valf();
 
 struct TrArgs {
@@ -539,7 +537,7 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
   // the epilogue walks 32-bit positions (token and document indices)
   constexpr int64_t kMax32 = 0x7fffffffLL - 64;
-  if (chunks < 1 || chunks > (split ? kTrMaxChunksSplit : kTrMaxChunks) || n_tokens > kMax32 ||
+  if (chunks < 1 || chunks > kTrMaxChunks || n_tokens > kMax32 ||
       n_docs > kMax32 || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
       K > 256 || cb_bytes > (split ? 128 : 96) * 1024 || n_tokens <= 0 ||
       (reinterpret_cast<uintptr_t>(Q) & 15))
@@ -596,7 +594,9 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   auto kern = split ? ((nch == 1)   ? pq_tokrows_kernel<1, true>
                        : (nch == 2) ? pq_tokrows_kernel<2, true>
                                     : pq_tokrows_kernel<4, true>)
-                    : ((nch == 1) ? pq_tokrows_kernel<1, false> : pq_tokrows_kernel<2, false>);
+                    : ((nch == 1)   ? pq_tokrows_kernel<1, false>
+                       : (nch == 2) ? pq_tokrows_kernel<2, false>
+                                    : pq_tokrows_kernel<4, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return TMS_ERR_CUDA;
