@@ -530,6 +530,12 @@ RES_CONFIGS = {
 }
 
 
+def res_score_launches(nqry: int, nq: int) -> int:
+    """Kernels one residual scoring call launches (csrc/dense_maxsim.cu tms_residual_maxsim)."""
+    nchunk = -(-nq // 32)
+    return (1 + (1 if nchunk > 1 else 0)) if nqry * nchunk <= 4 else 2
+
+
 def run_res(args, cfg, rank: int, world: int, device: torch.device) -> None:
     """Residual-compressed scoring (ResidualMaxSim.score_queries) + per-query top-k."""
     import tilemaxsim_b200 as tms
@@ -614,15 +620,17 @@ def run_res(args, cfg, rank: int, world: int, device: torch.device) -> None:
                                f"normalised), top-{k}",
                    "l2": "codes and residuals larger than L2"},
         "residual_kernel_ms": kern_ms, "residual_kernel_ms_p50_p95": percentiles(kern_list),
-        # the decoder warps (two per scheduler) are latency-bound: the compressed corpus streams at a
-        # small fraction of HBM bandwidth
+        # up to four query chunks: the token-rows kernel (decoded tokens written to TMEM as the MMA's
+        # A operand), bound by its TMEM traffic and the decode; the compressed corpus streams at a
+        # fraction of HBM bandwidth
         "roofline": {"bound": "hbm", "achieved": hbm_bytes / (kern_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": hbm_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"], "traffic": None,
-                     "note": "decode-latency bound, not HBM bound"},
+                     "note": "decode / TMEM bound, not HBM bound"},
         "e2e": {"value": pairs / (e2e_ms * 1e-3), "unit": "doc-tokens/s", "h2d_bytes_per_step": Qh.numel() * 2,
                 "d2h_bytes_per_step": nqry * k * 12, "ms_per_step": e2e_ms},
-        # packing + the decoder kernel per scoring call, then the top-k (and merge) kernels
-        "gpu_launches": search_launches(nqry, n_docs, k, world, 2) * args.steps,
+        # per scoring call: the token-rows kernel (+ the chunk sum for > 32-token queries) for up to
+        # four query chunks, else packing + the decoder kernel; then the top-k (and merge) kernels
+        "gpu_launches": search_launches(nqry, n_docs, k, world, res_score_launches(nqry, nq)) * args.steps,
         "clocks": clocks})
 
 

@@ -170,13 +170,26 @@ def test_full_size_rerank_consistency(cuda_device):
 
 
 @pytest.mark.parametrize("case", ["single_query", "multi_query", "pq_tensor", "pq_token_rows", "pq_precise",
-                                  "pq_precise4"])
+                                  "pq_precise4", "residual_rows"])
 def test_bounded_wait_reports_timeout(case, cuda_device):
     """Fault knob: the producer issues no load, so every consumer wait runs out after the (short)
     limit; the kernel returns, the host reads TMS_ERR_TIMEOUT, and the context stays usable."""
     from tilemaxsim_b200 import TileMaxSimPQ, _lib, maxsim_batched
     lib = _lib.load()
-    if case.startswith("pq"):
+    if case == "residual_rows":
+        from tilemaxsim_b200 import ResidualMaxSim
+        cent = torch.nn.functional.normalize(torch.randn(64, 128, generator=R.gen(4)), dim=-1).half()
+        codes = torch.randint(0, 64, (40 * 64,), generator=R.gen(4), dtype=torch.int32)
+        res = torch.randint(0, 256, (40 * 64, 32), generator=R.gen(4), dtype=torch.uint8)
+        bw = torch.tensor([-0.05, -0.01, 0.01, 0.05])
+        off = (torch.arange(41, dtype=torch.int64) * 64)
+        scorer = ResidualMaxSim(cent.to(cuda_device), bw.to(cuda_device), 2)
+        Qb = R.normalized((1, 32, 128), 5)
+        args = [Qb.to(cuda_device), codes.to(cuda_device), res.to(cuda_device), off.to(cuda_device)]
+        run = lambda: scorer.score_queries(*args)  # noqa: E731
+        want = O.maxsim_ragged(Qb, torch.from_numpy(O.residual_decompress(cent, codes, res, bw, 2)), off.numpy())
+        tol = (1e-3, 1e-3)
+    elif case.startswith("pq"):
         cb = R.randn((16, 256, 8), 3, torch.float32).to(cuda_device)
         pq = TileMaxSimPQ(cb, exact=case.startswith("pq_precise"))
         codes = torch.randint(0, 256, (40 * 64, 16), generator=R.gen(4), dtype=torch.uint8).to(cuda_device)

@@ -27,8 +27,12 @@ def _corpus(d, nbits, seed, n_docs=400, hi=150, n_cent=1000):
 
 @pytest.mark.parametrize("nqry,nq,nbits,normalize,d", [
     (1, 32, 2, True, 128), (5, 32, 2, True, 128), (3, 32, 1, False, 128), (2, 32, 4, True, 128),
-    (1, 40, 2, True, 128), (1, 32, 2, True, 64), (6, 20, 4, False, 64), (2, 32, 1, True, 64)])
+    (1, 40, 2, True, 128), (1, 32, 2, True, 64), (6, 20, 4, False, 64), (2, 32, 1, True, 64),
+    (4, 32, 2, True, 128), (1, 100, 4, True, 64), (2, 32, 2, False, 128)])
 def test_residual_vs_oracle(nqry, nq, nbits, normalize, d, cuda_device):
+    """Up to four 32-row query chunks take the token-rows kernel (decoded tokens in TMEM, one
+    document stream per lane, the unit-length scale applied to each token's products); larger
+    batches the dense kernel's residual decoder warps."""
     from tilemaxsim_b200 import ResidualMaxSim
     cent, codes, res, bw, off = _corpus(d, nbits, seed=nqry + 10 * nbits + d)
     Q = R.normalized((nqry, nq, d), 7)

@@ -1699,7 +1699,9 @@ extern "C" int tms_dense_maxsim_noalloc(const void* Q, int dtype, int64_t n_quer
 extern "C" size_t tms_residual_workspace_size(int64_t n_queries, int64_t nq, int64_t d,
                                               int64_t n_docs) {
   if (n_queries <= 0 || nq <= 0 || d <= 0 || d > 128 || d % 64 != 0 || n_docs < 0) return 0;
-  return tms_dense_workspace_size(TMS_F16, n_queries, nq, d, n_docs, TMS_OUT_SCORE);
+  const size_t dense = tms_dense_workspace_size(TMS_F16, n_queries, nq, d, n_docs, TMS_OUT_SCORE);
+  const size_t rows = tms::pq_tokrows_workspace_size(n_queries, nq, n_docs);  // token-rows kernel
+  return dense > rows ? dense : rows;
 }
 
 extern "C" int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,
@@ -1730,6 +1732,15 @@ extern "C" int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq,
     if (blocks > dev->num_sms * 8) blocks = dev->num_sms * 8;
     tms::fill_kernel<<<blocks, 256, 0, st>>>(out, total, tms::kNegInf);
     return tms::cuda_status(cudaGetLastError());
+  }
+  // up to four 32-row query chunks: the token-rows kernel (decoded tokens as the TMEM A operand,
+  // one document stream per lane); larger batches: the dense kernel's residual decoder warps
+  if (((nq + 31) / 32) * n_queries <= 4) {
+    const int rc = tms::res_tokrows_maxsim(Q, n_queries, nq, d, centroids, n_centroids, codes,
+                                           residuals, bucket_weights, nbits, normalize, n_tokens,
+                                           doc_offsets, n_docs, nd_uniform, out, workspace,
+                                           workspace_bytes, st);
+    if (rc != TMS_ERR_UNSUPPORTED) return rc;
   }
   return tms::decoder_maxsim<true>(
       Q, n_queries, nq, d, tms::residual_layout(static_cast<int>(d), nbits).total, n_tokens, doc_offsets, n_docs,

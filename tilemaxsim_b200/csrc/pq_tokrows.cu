@@ -65,7 +65,31 @@ struct TrArgs {
   int nslot;                 // TMEM slots (A columns + accumulator columns each)
   int n_ranges;
   int debug_flags;  // bit 0: decoders write nothing (exercises the bounded waits)
+  // residual-compressed corpora (modes kTrRes1/2/4): token t = centroids[rcodes[t]] + bucket
+  // weights of its residual row (rbytes bytes), scaled to unit length when normalize != 0
+  const __half* cent;
+  int64_t ncent;
+  const int32_t* rcodes;
+  const uint8_t* rbits;
+  const float* bucket_w;
+  int rbytes, normalize;
 };
+
+// Decoder modes (kernel template parameter): PQ with an fp16 codebook, PQ with the codebook split
+// into fp16 hi + lo, residual codes with 1, 2 or 4 bits per dimension.
+constexpr int kTrPq = 0, kTrPqSplit = 1, kTrRes1 = 2, kTrRes2 = 3, kTrRes4 = 4;
+// Residual mode: a 16-entry table of bucket weights per 4 residual bits (4 / nbits dimensions an
+// entry), the decoders' partial sums of squares per (slot, lane quarter, half, lane), and each
+// decoder warp's ring of kTrResRing tiles: per lane its token's centroid half-row (pitch
+// d + 16 bytes) and residual half-row (pitch tr_res_pb: conflict-free vector reads).
+constexpr int kTrResRing = 3;
+__host__ __device__ inline int tr_res_pb(int rw) { return rw == 8 ? 48 : 4 * rw; }
+__host__ __device__ inline uint32_t tr_res_slot(int d, int nb) {
+  return 32u * static_cast<uint32_t>(d + 16 + tr_res_pb(d / 2 * nb / 32));
+}
+__host__ __device__ inline uint32_t tr_res_bytes(int nslot, int d, int nb) {
+  return 256u + static_cast<uint32_t>(nslot) * 4u * 2u * 32u * 4u + 8u * kTrResRing * tr_res_slot(d, nb);
+}
 
 struct TrLayout {
   uint32_t b_off, cb_off, bar_off, misc_off, total;
@@ -164,16 +188,19 @@ template <int NCH> struct TrShape {
   static constexpr int kEpiChunks = NCH > 2 ? NCH / 2 : NCH;  // chunks per epilogue warp
 };
 
-template <int NCH, bool SPLIT>
+template <int NCH, int MODE>
 __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs a) {
   using Shape = TrShape<NCH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int N = NCH * 32;
+  constexpr bool SPLIT = MODE == kTrPqSplit;
+  constexpr bool RES = MODE >= kTrRes1;
+  constexpr int NB = RES ? (1 << (MODE - kTrRes1)) : 0;  // residual bits per dimension
   // TMEM columns of one decoded tile (fp16 pairs): d, or 2d for [hi | lo] rows
   const int acols = a.d / 2 * (SPLIT ? 2 : 1);
   const int S = a.nslot;
-  const int n_cb = a.M * a.K * a.dsub;  // codebook elements (one table; the lo table follows)
-  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(n_cb * 2 * (SPLIT ? 2 : 1)), S);
+  const int n_cb = RES ? 0 : a.M * a.K * a.dsub;  // codebook elements (one table; the lo table follows)
+  const TrLayout L = tr_layout(N, a.d, RES ? tr_res_bytes(S, a.d, NB) : static_cast<uint32_t>(n_cb * 2 * (SPLIT ? 2 : 1)), S);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t b_s = sbase + L.b_off;
   const uint32_t bar_s = sbase + L.bar_off;
@@ -227,9 +254,23 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       misc->n_tiles = 0;
     }
   }
-  // Stage the codebook as fp16 and the query rows as the swizzled B operand (every thread helps).
+  // Stage the codebook as fp16 (PQ) or the bucket-weight table (residual), and the query rows as
+  // the swizzled B operand (every thread helps).
   {
-    const int n = a.M * a.K * a.dsub;
+    if constexpr (RES) {
+      // entry e (4 residual bits, most significant first = the lowest bit position) holds the
+      // weights of the G = 4 / NB dimensions those bits encode: dimension g's bucket index has
+      // bit k = bit 3 - (g NB + k) of e
+      constexpr int G = 4 / NB;
+      float* tab = reinterpret_cast<float*>(smem + L.cb_off);
+      for (int i = threadIdx.x; i < 16 * G; i += blockDim.x) {
+        const int e = i / G, g = i - e * G;
+        int b = 0;
+        for (int k = 0; k < NB; ++k) b |= ((e >> (3 - (g * NB + k))) & 1) << k;
+        tab[i] = __ldg(a.bucket_w + b);
+      }
+    }
+    const int n = n_cb;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       float v;
       if (a.cb_dtype == TMS_F16) v = __half2float(reinterpret_cast<const __half*>(a.codebook)[i]);
@@ -238,7 +279,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       const __half hi = __float2half_rn(v);
       cbs[i] = hi;
       // the rounding error of hi, itself rounded to fp16: hi + lo carries ~22 significant bits
-      if (SPLIT) cbs[n + i] = __float2half_rn(v - __half2float(hi));
+      if constexpr (SPLIT) cbs[n + i] = __float2half_rn(v - __half2float(hi));
     }
     const int upr = a.d / 8;  // 16-byte units per query row
     for (int i = threadIdx.x; i < N * upr; i += blockDim.x) {
@@ -331,10 +372,164 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
     const int q = warp & 3;
     const int hp = (warp - kTrDecWarp0) >> 2;
     const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    auto nothing = [](int) {};
+    if constexpr (RES) {
+    // Residual decoding: warp hp rebuilds dimensions [hp d/2, (hp + 1) d/2) of its 32 tokens from
+    // the centroid row and the residual bits (weights from the 16-entry table, 4 bits at a time),
+    // rounds them once to fp16 into TMEM, and leaves the half's sum of squares in shared memory:
+    // the epilogue scales each token's products by its inverse norm. Each lane copies its token's
+    // centroid half-row (read through L2) and residual half-row into the warp's ring with cp.async
+    // kTrResRing tiles ahead (its centroid id loaded a tile before that), so the decode reads
+    // shared memory only.
+    const int DH = a.d / 2;       // 32 or 64 dimensions
+    const int UN = DH / 8;        // 16-byte centroid units: 4 or 8
+    const int RW = DH * NB / 32;  // 32-bit residual words: 1 .. 8
+    const int CP = 2 * DH + 16, PB = tr_res_pb(RW);
+    const float* tab = reinterpret_cast<const float*>(smem + L.cb_off);
+    float* nrm = reinterpret_cast<float*>(smem + L.cb_off + 256);
+    const uint32_t slot_bytes = tr_res_slot(a.d, NB);
+    uint8_t* ring = smem + L.cb_off + 256 + S * 1024 + (warp - kTrDecWarp0) * kTrResRing * slot_bytes;
+    const uint32_t ring_s = smem_u32(ring);
+    const uintptr_t rb_addr = reinterpret_cast<uintptr_t>(a.rbits);
+    const bool wide16 = RW >= 4 && (rb_addr & 15) == 0;
+    const bool wide8 = RW == 2 && (rb_addr & 7) == 0;
+    LaneDocs<true> ls;
+    ls.init(docs, misc->sub_doc[q], static_cast<int>(misc->sub_doc[q + 1] - misc->sub_doc[q]), lane, nothing);
+    struct Ahead {
+      int64_t pos;
+      int32_t code;
+      bool in;
+    };
+    auto take = [&]() -> Ahead {
+      Ahead t;
+      t.in = ls.active() && ls.pos >= 0 && ls.pos < a.n_tokens;
+      t.pos = ls.pos;
+      t.code = t.in ? __ldg(a.rcodes + ls.pos) : 0;
+      ls.step(docs, nothing, nothing);
+      return t;
+    };
+    // copies of tile t's rows into ring slot t % kTrResRing (one commit group per tile)
+    auto issue = [&](const Ahead& t, int r) {
+      int64_t c = t.code;
+      c = c < 0 ? 0 : (c >= a.ncent ? a.ncent - 1 : c);  // never outside the table
+      const __half* csrc = a.cent + c * a.d + hp * DH;
+      const uint32_t cdst = ring_s + r * slot_bytes + lane * CP;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < UN) cp_async16(cdst + 16u * u, csrc + 8 * u);
+      if (t.in) {
+        const uint8_t* bsrc = a.rbits + t.pos * a.rbytes + hp * (a.rbytes / 2);
+        const uint32_t bdst = ring_s + r * slot_bytes + 32 * CP + lane * PB;
+        if (wide16) {
+          for (int w4 = 0; w4 < RW / 4; ++w4) cp_async16(bdst + 16u * w4, bsrc + 16 * w4);
+        } else if (wide8) {
+          cp_async8(bdst, bsrc);
+        } else {
+          for (int w1 = 0; w1 < RW; ++w1) cp_async4(bdst + 4u * w1, bsrc + 4 * w1);
+        }
+      }
+      cp_async_commit();
+    };
+    bool ok = !(a.debug_flags & 1);
+    if (ok) {
+#pragma unroll
+      for (int t = 0; t < kTrResRing; ++t) {
+        const Ahead A = take();
+        if (t < n_tiles) issue(A, t);
+        else cp_async_commit();
+      }
+    }
+    Ahead C = take();  // the tile kTrResRing ahead of the decode
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int s = j % S;
+      const int r = j % kTrResRing;
+      int w = 0;
+      if (lane == 0) w = mbar_wait(free_bar(s), ((j / S) & 1u) ^ 1u, abort_flag, tmo, a.err, 23);
+      if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+      cp_async_wait_group<kTrResRing - 1>();  // this lane's copies of tile j have landed
+      const uint8_t* crow = ring + r * slot_bytes + lane * CP;
+      const uint8_t* brow = ring + r * slot_bytes + 32 * CP + lane * PB;
+      uint32_t bits[8];
+      if (RW >= 4) {
+#pragma unroll
+        for (int w4 = 0; w4 < 2; ++w4)
+          if (4 * w4 < RW) {
+            const uint4 v = *reinterpret_cast<const uint4*>(brow + 16 * w4);
+            bits[4 * w4] = v.x;
+            bits[4 * w4 + 1] = v.y;
+            bits[4 * w4 + 2] = v.z;
+            bits[4 * w4 + 3] = v.w;
+          }
+      } else if (RW == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(brow);
+        bits[0] = v.x;
+        bits[1] = v.y;
+      } else {
+        bits[0] = *reinterpret_cast<const uint32_t*>(brow);
+      }
+      uint32_t out[32];
+      uint64_t ss = 0ull;  // a pair of partial sums of squares
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (u < UN) {
+          // unit u: dimensions 8u .. 8u + 7 of the half = residual nibbles 2u NB .. 2u NB + 2NB - 1
+          // (bit positions in order: the high nibble of a byte first)
+          float wt[8];
+#pragma unroll
+          for (int k = 0; k < 2 * NB; ++k) {
+            const int n = 2 * u * NB + k;
+            const int byte = n >> 1;
+            const uint32_t e = (bits[byte >> 2] >> (8 * (byte & 3) + ((n & 1) ? 0 : 4))) & 0xFu;
+            if constexpr (NB == 1) {
+              const float4 t4 = *reinterpret_cast<const float4*>(tab + 4 * e);
+              wt[4 * k] = t4.x;
+              wt[4 * k + 1] = t4.y;
+              wt[4 * k + 2] = t4.z;
+              wt[4 * k + 3] = t4.w;
+            } else if constexpr (NB == 2) {
+              const float2 t2 = *reinterpret_cast<const float2*>(tab + 2 * e);
+              wt[2 * k] = t2.x;
+              wt[2 * k + 1] = t2.y;
+            } else {
+              wt[k] = tab[e];
+            }
+          }
+          const uint4 cu = *reinterpret_cast<const uint4*>(crow + 16 * u);
+          const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w};
+#pragma unroll
+          for (int p2 = 0; p2 < 4; ++p2) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cw[p2]));
+            const uint64_t x = f2_add(f2_pack(f.x, f.y), f2_pack(wt[2 * p2], wt[2 * p2 + 1]));
+            ss = f2_fma(x, x, ss);
+            const float2 v = f2_unpack(x);
+            const __half2 h = __floats2half2_rn(v.x, v.y);
+            out[4 * u + p2] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+      }
+      if (DH == 64) tmem_st32(t_quarter + a_col(s) + 32u * hp, out);
+      else tmem_st16(t_quarter + a_col(s) + 16u * hp, out);
+      const float2 sp = f2_unpack(ss);
+      nrm[((s * 4 + q) * 2 + hp) * 32 + lane] = sp.x + sp.y;
+      // slot r is read (the stores above consumed it): refill it with tile j + kTrResRing
+      if (j + kTrResRing < n_tiles) issue(C, r);
+      else cp_async_commit();
+      C = take();
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (!Shape::kMmaInDecoder) {
+        if (lane == 0) mbar_arrive(afull_bar(s));
+      } else if (lane == 0 && (count_arrival(&misc->arrivals[s]) & 7u) == 7u) {
+        tc_fence_after();
+        mma_tile(s);
+      }
+    }
+    cp_async_wait_all();  // no copy into the ring outlives the kernel
+    } else {
     // d = 128, M = 16, dsub = 8: warp hp needs code bytes [8 hp, 8 hp + 8) of each token
     const bool fast = (a.M == 16) && (a.dsub == 8) && ((reinterpret_cast<uintptr_t>(a.codes) & 15) == 0);
     const uint32_t kmax = static_cast<uint32_t>(a.K - 1);
-    auto nothing = [](int) {};
     // The stream runs two tiles ahead of the decode in the fast case (codes of the next two
     // tiles in flight), level with it otherwise (codes read inside the decode).
     LaneDocs<true> ls;
@@ -424,6 +619,7 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
         mma_tile(s);
       }
     }
+    }
     // each decoder warp commits once: done_bar completes when every MMA it issued has landed
     if (Shape::kMmaInDecoder && lane == 0) mma_commit(done_bar);
   } else if (warp >= kTrEpiWarp0 || (Shape::kEpiWarps == 8 && warp < 4)) {
@@ -463,6 +659,23 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
       tc_fence_after();
       const bool act = ls.active();
+      // residual corpora scaled to unit length: this lane's token's inverse norm, from the two
+      // decoder halves' sums of squares (read before the slot is handed back; the decoders
+      // published them before their tile hand-off, which this acquires)
+      float inv = 1.0f;
+      if (RES && a.normalize) {
+        if (Shape::kMmaInDecoder) {
+          cuda::atomic_ref<uint32_t, cuda::thread_scope_block> ctr(misc->arrivals[s]);
+          (void)ctr.load(cuda::memory_order_acquire);
+        } else {
+          if (lane == 0) w = mbar_wait(afull_bar(s), (j / S) & 1u, abort_flag, tmo, a.err, 25);
+          if (!(ok = __shfl_sync(0xffffffffu, w, 0) != 0)) break;
+          __syncwarp();  // lane 0's acquire orders the other lanes' reads below
+        }
+        const float* nrm = reinterpret_cast<const float*>(smem + L.cb_off + 256) + (s * 4 + q) * 64 + lane;
+        const float ssq = nrm[0] + nrm[32];
+        inv = ssq > 0.0f ? rsqrtf(ssq) : 0.0f;
+      }
 #pragma unroll
       for (int c = 0; c < EC; ++c) {
         uint32_t r[32];
@@ -474,7 +687,10 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
           if (lane == 0) mbar_arrive(free_bar(s));
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[c][i] = act ? fmaxf(acc[c][i], __uint_as_float(r[i])) : acc[c][i];
+        for (int i = 0; i < 32; ++i) {
+          const float v = RES ? __uint_as_float(r[i]) * inv : __uint_as_float(r[i]);
+          acc[c][i] = act ? fmaxf(acc[c][i], v) : acc[c][i];
+        }
       }
       // a document ends on this lane: its scores (summed by the whole warp, a uniform branch, so
       // that no divergent region holds the accumulators), then the stream moves on
@@ -526,21 +742,25 @@ size_t pq_tokrows_workspace_size(int64_t n_queries, int64_t nq, int64_t n_docs) 
   return nchunk > 1 ? align_up(static_cast<size_t>(n_queries * nchunk * n_docs) * 4, 256) : 0;
 }
 
-int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook,
-                      int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
-                      int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
-                      int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
-                      cudaStream_t st, bool split) {
-  const int64_t d = M * dsub;
+namespace {
+
+using TrKernel = void (*)(TrArgs);
+template <int MODE>
+TrKernel tr_kernel(int nch) {
+  return nch == 1 ? pq_tokrows_kernel<1, MODE> : (nch == 2 ? pq_tokrows_kernel<2, MODE> : pq_tokrows_kernel<4, MODE>);
+}
+
+// the epilogue walks 32-bit positions (token and document indices)
+constexpr int64_t kTrMax32 = 0x7fffffffLL - 64;
+
+// Shared by the PQ and residual entry points: a.d, a.nq and the source fields set by the caller.
+int tr_launch(TrArgs& a, int mode, int64_t n_queries, int64_t nq, int64_t n_tokens,
+              const int64_t* doc_offsets, int64_t n_docs, int64_t nd_uniform, float* out,
+              void* workspace, size_t workspace_bytes, cudaStream_t st, int acols,
+              uint32_t fixed_bytes) {
   const int64_t nchunk = (nq + 31) / 32;
   const int64_t chunks = n_queries * nchunk;
-  const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
-  // the epilogue walks 32-bit positions (token and document indices)
-  constexpr int64_t kMax32 = 0x7fffffffLL - 64;
-  if (chunks < 1 || chunks > kTrMaxChunks || n_tokens > kMax32 ||
-      n_docs > kMax32 || d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 ||
-      K > 256 || cb_bytes > (split ? 128 : 96) * 1024 || n_tokens <= 0 ||
-      (reinterpret_cast<uintptr_t>(Q) & 15))
+  if (chunks < 1 || chunks > kTrMaxChunks || n_tokens > kTrMax32 || n_docs > kTrMax32 || n_tokens <= 0)
     return TMS_ERR_UNSUPPORTED;
   int status = TMS_OK;
   const DeviceInfo* dev = current_device_info(&status);
@@ -548,7 +768,6 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   // the kernel's query tile is NCH x 32 rows: three chunks run on the four-chunk kernel
   const int nch = chunks > 2 ? 4 : static_cast<int>(chunks);
   const int N = nch * 32;
-  const int acols = static_cast<int>(d / 2) * (split ? 2 : 1);
   // as many slots as TMEM holds: a hand-off through an mbarrier takes ~500 cycles, so several
   // tiles must be in flight between the decoders, the MMA and the epilogue
   int nslot = 512 / (acols + N);
@@ -556,23 +775,13 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   if (nslot < 2 || nslot * (acols + N) > 512) return TMS_ERR_UNSUPPORTED;
   const size_t need = pq_tokrows_workspace_size(n_queries, nq, n_docs);
   if (need && (!workspace || workspace_bytes < need)) return TMS_ERR_WORKSPACE;
-  TrArgs a;
   a.docs.offsets = doc_offsets;
   a.docs.n_docs = n_docs;
   a.docs.nd = doc_offsets ? 0 : nd_uniform;
-  a.codes = codes;
   a.n_tokens = n_tokens;
-  a.Q = static_cast<const __half*>(Q);
-  a.codebook = codebook;
   a.out = nchunk > 1 ? static_cast<float*>(workspace) : out;
   a.err = dev->err_word;
   a.timeout_ns = wait_timeout_ns();
-  a.cb_dtype = cb_dtype;
-  a.M = static_cast<int>(M);
-  a.K = static_cast<int>(K);
-  a.dsub = static_cast<int>(dsub);
-  a.d = static_cast<int>(d);
-  a.nq = static_cast<int>(nq);
   a.nchunk = static_cast<int>(nchunk);
   a.n_chunks = static_cast<int>(chunks);
   a.nslot = nslot;
@@ -584,19 +793,23 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   if (ranges > n_docs) ranges = n_docs;
   if (ranges < 1) ranges = 1;
   a.n_ranges = static_cast<int>(ranges);
-  const TrLayout L = tr_layout(N, a.d, static_cast<uint32_t>(cb_bytes), nslot);
+  const uint32_t cb_bytes =
+      mode >= kTrRes1 ? tr_res_bytes(nslot, a.d, 1 << (mode - kTrRes1)) : fixed_bytes;
+  const TrLayout L = tr_layout(N, a.d, cb_bytes, nslot);
   // at least half the SM's shared memory: one CTA per SM, so the 512-column TMEM allocation
   // never waits for another CTA
   size_t smem = L.total;
   const size_t half = static_cast<size_t>(dev->max_smem_optin) / 2 + 1024;
   if (smem < half) smem = half;
   if (static_cast<int>(smem) > dev->max_smem_optin) return TMS_ERR_UNSUPPORTED;
-  auto kern = split ? ((nch == 1)   ? pq_tokrows_kernel<1, true>
-                       : (nch == 2) ? pq_tokrows_kernel<2, true>
-                                    : pq_tokrows_kernel<4, true>)
-                    : ((nch == 1)   ? pq_tokrows_kernel<1, false>
-                       : (nch == 2) ? pq_tokrows_kernel<2, false>
-                                    : pq_tokrows_kernel<4, false>);
+  TrKernel kern = nullptr;
+  switch (mode) {
+    case kTrPq: kern = tr_kernel<kTrPq>(nch); break;
+    case kTrPqSplit: kern = tr_kernel<kTrPqSplit>(nch); break;
+    case kTrRes1: kern = tr_kernel<kTrRes1>(nch); break;
+    case kTrRes2: kern = tr_kernel<kTrRes2>(nch); break;
+    default: kern = tr_kernel<kTrRes4>(nch); break;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return TMS_ERR_CUDA;
@@ -609,6 +822,59 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
   tr_sum_chunks_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(workspace), out, n_queries,
                                                n_docs, static_cast<int>(nchunk));
   return cuda_status(cudaGetLastError());
+}
+
+}  // namespace
+
+int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* codebook,
+                      int cb_dtype, int64_t M, int64_t K, int64_t dsub, const uint8_t* codes,
+                      int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
+                      int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
+                      cudaStream_t st, bool split) {
+  const int64_t d = M * dsub;
+  const size_t cb_bytes = static_cast<size_t>(M * K * dsub) * 2 * (split ? 2 : 1);
+  if (d % 64 != 0 || d > 256 || dsub % 8 != 0 || K < 1 || K > 256 ||
+      cb_bytes > (split ? 128 : 96) * 1024 || (reinterpret_cast<uintptr_t>(Q) & 15))
+    return TMS_ERR_UNSUPPORTED;
+  TrArgs a = {};
+  a.codes = codes;
+  a.Q = static_cast<const __half*>(Q);
+  a.codebook = codebook;
+  a.cb_dtype = cb_dtype;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.dsub = static_cast<int>(dsub);
+  a.d = static_cast<int>(d);
+  a.nq = static_cast<int>(nq);
+  return tr_launch(a, split ? kTrPqSplit : kTrPq, n_queries, nq, n_tokens, doc_offsets, n_docs,
+                   nd_uniform, out, workspace, workspace_bytes, st,
+                   static_cast<int>(d / 2) * (split ? 2 : 1), static_cast<uint32_t>(cb_bytes));
+}
+
+int res_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,
+                       const void* centroids, int64_t n_centroids, const int32_t* codes,
+                       const uint8_t* residuals, const float* bucket_weights, int nbits,
+                       int normalize, int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
+                       int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
+                       cudaStream_t st) {
+  if ((d != 64 && d != 128) || (nbits != 1 && nbits != 2 && nbits != 4) || n_centroids < 1 ||
+      (reinterpret_cast<uintptr_t>(Q) & 15) || (reinterpret_cast<uintptr_t>(centroids) & 15) ||
+      (reinterpret_cast<uintptr_t>(residuals) & 3) || (reinterpret_cast<uintptr_t>(codes) & 3))
+    return TMS_ERR_UNSUPPORTED;
+  TrArgs a = {};
+  a.Q = static_cast<const __half*>(Q);
+  a.d = static_cast<int>(d);
+  a.nq = static_cast<int>(nq);
+  a.cent = static_cast<const __half*>(centroids);
+  a.ncent = n_centroids;
+  a.rcodes = codes;
+  a.rbits = residuals;
+  a.bucket_w = bucket_weights;
+  a.rbytes = static_cast<int>(d * nbits / 8);
+  a.normalize = normalize ? 1 : 0;
+  const int mode = nbits == 1 ? kTrRes1 : (nbits == 2 ? kTrRes2 : kTrRes4);
+  return tr_launch(a, mode, n_queries, nq, n_tokens, doc_offsets, n_docs, nd_uniform, out,
+                   workspace, workspace_bytes, st, static_cast<int>(d / 2), 0u);
 }
 
 }  // namespace tms

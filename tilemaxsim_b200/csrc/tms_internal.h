@@ -69,5 +69,13 @@ int pq_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, const void* 
                       int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
                       int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
                       cudaStream_t st, bool split);
+// Residual-compressed corpora on the token-rows kernel (up to four 32-row query chunks, d = 64 or
+// 128); TMS_ERR_UNSUPPORTED for other shapes (the caller then takes the dense decoder kernel).
+int res_tokrows_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,
+                       const void* centroids, int64_t n_centroids, const int32_t* codes,
+                       const uint8_t* residuals, const float* bucket_weights, int nbits,
+                       int normalize, int64_t n_tokens, const int64_t* doc_offsets, int64_t n_docs,
+                       int64_t nd_uniform, float* out, void* workspace, size_t workspace_bytes,
+                       cudaStream_t st);
 
 }  // namespace tms
