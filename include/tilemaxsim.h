@@ -55,9 +55,11 @@ extern "C" {
 #define TMS_PQ_FAST 0  /* tensor cores where the shape allows (fp16 codebook) */
 #define TMS_PQ_EXACT 1 /* fp32 table lookups, the reference precision */
 #define TMS_PQ_PRECISE 2 /* the reference precision, by the fastest kernel that keeps it (Python
-                            default): fp16 queries of 1-2 chunks of 32 rows on the tensor cores
-                            with the codebook split into fp16 hi + lo (|codebook| < 65504, the
-                            caller's guarantee), everything else by the fp32 table lookups */
+                            default): fp16 queries of up to 128 rows on the tensor cores with the
+                            codebook split into fp16 hi + lo (|codebook| < 65504, the caller's
+                            guarantee), in passes of up to four 32-row chunks; batches of <= 8-row
+                            queries needing several passes, and other shapes, by the fp32 table
+                            lookups */
 
 /* dense output modes */
 #define TMS_OUT_SCORE 0     /* out[q * n_docs + doc] = sum_i max_j <Q_qi, D_j>                 */
@@ -133,8 +135,8 @@ TMS_API size_t tms_pq_workspace_size(int64_t n_queries, int64_t nq, int64_t M, i
  * out[q * n_docs + doc] = sum_i max_j sum_m table[q,i,m,codes[j,m]] (K <= 256).
  * mode TMS_PQ_FAST: fp16 queries with dsub % 8 == 0, M*dsub % 64 == 0 and a codebook of <= 96 KB
  * in fp16 run on the tensor cores (codes decoded on chip through the codebook rounded to fp16,
- * never written to HBM; |error| <= 1e-3*|score| + 5e-3): up to two 32-row query chunks
- * (n_queries * ceil(nq / 32) <= 2, d <= 256) with the decoded tokens written to tensor memory,
+ * never written to HBM; |error| <= 1e-3*|score| + 5e-3): up to four 32-row query chunks
+ * (n_queries * ceil(nq / 32) <= 4, d <= 256) with the decoded tokens written to tensor memory,
  * larger batches with the tokens decoded into shared memory; other shapes fall back to:
  * mode TMS_PQ_EXACT: the fp32 distance table of eight query tokens is built in shared memory and
  * table entries are summed straight from the codes (the reference's arithmetic; M = 8 or 16 with
@@ -176,7 +178,9 @@ TMS_API size_t tms_residual_workspace_size(int64_t n_queries, int64_t nq, int64_
  * index: bit k of b_j is bit (j*nbits + k) of the token's residual row, bits numbered from the most
  * significant bit of byte 0 (residuals: n_tokens x d*nbits/8 bytes; nbits 1, 2 or 4). Tokens are
  * decoded on chip, rounded once to fp16 and scored like tms_dense_maxsim (fp16 queries, fp32
- * accumulation; offsets or nd_uniform as there): out[q * n_docs + doc]. centroids: (n_centroids, d)
+ * accumulation; offsets or nd_uniform as there): out[q * n_docs + doc]. Up to four 32-row query
+ * chunks run on the token-rows kernel, which rounds the unscaled token to fp16 and applies the
+ * unit-length scale to the token's fp32 products; larger batches scale before rounding. centroids: (n_centroids, d)
  * fp16, 16-byte aligned; codes int32 (clamped to [0, n_centroids)); bucket_weights: 2^nbits fp32.
  * d = 64 or 128. The workspace must be 1024-byte aligned. */
 TMS_API int tms_residual_maxsim(const void* Q, int64_t n_queries, int64_t nq, int64_t d,

@@ -7,14 +7,15 @@ neither the (Nq, M, K) table nor an int32 copy of the codes is written to HBM (t
 both). ``score_queries`` is the additive multi-query, ragged-corpus entry point. By default
 (``exact=True``) scoring keeps the reference's precision, agreeing with its ADC path to fp32
 rounding (1e-5 relative): each CTA builds an fp32 distance table for eight query tokens in shared
-memory and sums table entries straight from the uint8 codes (no reconstruction); one or two fp16
-queries of up to 32 tokens (one of up to 64) instead run on the tensor cores with each token
-rebuilt from the codebook split into fp16 hi + fp16 lo parts, which carry about 22 significant
-bits (the codebook must lie inside the fp16 range, checked at construction; otherwise the table
-lookups take every shape).
+memory and sums table entries straight from the uint8 codes (no reconstruction); fp16 queries of
+up to 128 tokens instead run on the tensor cores, in passes of up to four 32-row query chunks, with
+each token rebuilt from the codebook split into fp16 hi + fp16 lo parts, which carry about 22
+significant bits (the codebook must lie inside the fp16 range, checked at construction; otherwise
+the table lookups take every shape; batches of <= 8-token queries that need several passes keep
+the table lookups too).
 ``exact=False`` is the faster tensor-core mode: queries in fp16 (fp32 / bf16 ones are rounded to
-fp16) and each token rebuilt on chip from an fp16 copy of the codebook; for one or two 32-row query
-chunks the rebuilt tokens go to tensor memory as the MMA's A operand (token-rows kernel), for
+fp16) and each token rebuilt on chip from an fp16 copy of the codebook; for up to four 32-row
+query chunks the rebuilt tokens go to tensor memory as the MMA's A operand (token-rows kernel), for
 larger batches into the dense kernel's shared-memory operand tiles. Rounding the codebook to fp16
 costs about 1e-3 relative (|error| <= 1e-3*|score| + 5e-3).
 ``pytorch_pqsim_baseline`` is the reference's decompress-then-score PyTorch baseline (:283-313).
