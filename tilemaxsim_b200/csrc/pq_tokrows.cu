@@ -409,15 +409,18 @@ __global__ void __launch_bounds__(kTrThreads, 1) pq_tokrows_kernel(const TrArgs 
       return t;
     };
     // copies of tile t's rows into ring slot t % kTrResRing (one commit group per tile)
+    // A lane whose stream has ended copies nothing: its ring slot keeps stale rows, which decode
+    // into its own TMEM row only, and the epilogue never reads that lane (copying any fixed row
+    // instead sent every idle lane of every SM to one L2 line).
     auto issue = [&](const Ahead& t, int r) {
-      int64_t c = t.code;
-      c = c < 0 ? 0 : (c >= a.ncent ? a.ncent - 1 : c);  // never outside the table
-      const __half* csrc = a.cent + c * a.d + hp * DH;
-      const uint32_t cdst = ring_s + r * slot_bytes + lane * CP;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (u < UN) cp_async16(cdst + 16u * u, csrc + 8 * u);
       if (t.in) {
+        int64_t c = t.code;
+        c = c < 0 ? 0 : (c >= a.ncent ? a.ncent - 1 : c);  // never outside the table
+        const __half* csrc = a.cent + c * a.d + hp * DH;
+        const uint32_t cdst = ring_s + r * slot_bytes + lane * CP;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (u < UN) cp_async16(cdst + 16u * u, csrc + 8 * u);
         const uint8_t* bsrc = a.rbits + t.pos * a.rbytes + hp * (a.rbytes / 2);
         const uint32_t bdst = ring_s + r * slot_bytes + 32 * CP + lane * PB;
         if (wide16) {
