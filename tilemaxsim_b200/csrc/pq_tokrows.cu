@@ -1,5 +1,6 @@
-// pq_tokrows.cu -- PQ-ADC on the sm_100a tensor cores for small query batches (up to four
-// 32-row query chunks), with the document tokens on the TMEM lanes.
+// pq_tokrows.cu -- PQ-ADC and residual-compressed (ColBERTv2) corpora on the sm_100a tensor
+// cores for small query batches (up to four 32-row query chunks), with the document tokens on the
+// TMEM lanes.
 //
 //   score[q, doc] = sum_i max_{j in doc} sum_m <Q[q,i,m*dsub:(m+1)*dsub], C[m, codes[j,m], :]>
 //
@@ -12,8 +13,11 @@
 // Design (the single-query PQ hot path):
 //  * Decoded tokens are the MMA's A operand: M = 128 token rows x K = d, written from registers
 //    straight into TMEM with tcgen05.st (lane = token, 32-bit column c = fp16 elements 2c, 2c+1).
-//    No shared-memory store and no replicated query tile: the only shared-memory traffic per token
-//    is the codebook gather (M random 16-byte reads at dsub = 8), which bounds the kernel.
+//    No shared-memory store and no replicated query tile: the shared-memory traffic per token is
+//    the codebook gather (M random 16-byte reads at dsub = 8). What paces the kernel is the MMA
+//    reading its A operand from TMEM beside the decoders' stores and the epilogue's loads.
+//    Residual corpora (modes kTrRes*): the decoders rebuild tokens from a centroid row and the
+//    residual bits instead of codebook rows; the rest of the kernel is shared.
 //  * The query rows are the B operand (N = 32, 64 or 128), resident in shared memory in the 128-byte-
 //    swizzle K-major layout. S^T = Dtile . Q^T lands with one token per TMEM lane and one query row
 //    per column.
@@ -32,8 +36,8 @@
 // Warp roles (one or two chunks, 512 threads): warp 1 = TMEM owner + MMA issuer; warps 4..11 =
 // decoders (lane quarter = warp % 4; the quarter's two warps rebuild alternate 64-element column
 // blocks of every tile); warps 12..15 = epilogue (lane quarter = warp % 4); warps 0, 2, 3 only
-// help in the prologue. Three or four chunks: warps 0..3 are a second
-// epilogue group and warp 4, a decoder, also issues the MMAs (TrShape).
+// help in the prologue. Three or four chunks: warps 0..3 are a second epilogue group and the
+// last decoder warp to finish a tile issues its MMAs (TrShape).
 #include <cuda/atomic>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
