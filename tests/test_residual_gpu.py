@@ -124,3 +124,27 @@ def test_residual_colbert_encoded_corpus(nbits, cuda_device):
     bound = torch.linalg.vector_norm(Q.float(), dim=-1).sum(-1).numpy()[:, None] * per_doc[None, :]
     exact = O.maxsim_ragged(Q, torch.from_numpy(X), off)
     assert np.all(np.abs(got - exact) <= bound + 1e-3)
+
+
+@pytest.mark.parametrize("nqry", [1, 5])
+def test_residual_offsets_not_starting_at_zero(nqry, cuda_device):
+    """A corpus given as a window of larger code / residual arrays (offsets start past 0), on the
+    token-rows kernel (one query) and the dense kernel's decoder warps (five queries)."""
+    from tilemaxsim_b200 import ResidualMaxSim
+    cent, codes, res, bw, off = _corpus(128, 2, seed=31 + nqry, n_docs=500)
+    pad = 777
+    T = codes.numel()
+    codes_w = torch.cat([torch.randint(0, cent.shape[0], (pad,), generator=R.gen(1), dtype=torch.int32), codes,
+                         torch.zeros(40, dtype=torch.int32)])
+    res_w = torch.cat([torch.randint(0, 256, (pad, res.shape[1]), generator=R.gen(2), dtype=torch.uint8), res,
+                       torch.zeros(40, res.shape[1], dtype=torch.uint8)])
+    off_w = off + pad
+    Q = R.normalized((nqry, 32, 128), 12)
+    scorer = ResidualMaxSim(cent.to(cuda_device), bw.to(cuda_device), 2)
+    got = scorer.score_queries(Q.to(cuda_device), codes_w.to(cuda_device), res_w.to(cuda_device),
+                               torch.from_numpy(off_w).to(cuda_device)).cpu().numpy()
+    assert codes_w.numel() == T + pad + 40
+    want = O.maxsim_ragged(Q, torch.from_numpy(O.residual_decompress(cent, codes, res, bw, 2)), off)
+    inf = np.isinf(want)
+    np.testing.assert_array_equal(got[inf], want[inf])
+    np.testing.assert_allclose(got[~inf], want[~inf], rtol=1e-3, atol=1e-3)
