@@ -104,3 +104,28 @@ def test_residual_scorer_validates_before_any_kernel():
     res = torch.zeros(10, 32, dtype=torch.uint8)
     with pytest.raises(ValueError, match="CUDA"):
         sc.score_queries(Q, codes, res, torch.tensor([0, 10]))
+
+
+@pytest.mark.parametrize("nqry,nq,exact,route,launches", [
+    (16, 32, True, "tokrows", 4),   # C4 at the reference precision: four passes of four queries
+    (1, 32, True, "tokrows", 1),    # single query, hi/lo token rows
+    (5, 40, True, "tokrows", 6),    # 2 + 2 + 1 queries of two chunks: three passes + chunk sums
+    (6, 8, True, "lut", 1),         # <= 8-token queries needing several passes: table lookups
+    (1, 32, False, "tokrows", 1),   # fast mode, one chunk
+    (4, 32, False, "tokrows", 1),   # fast mode, four chunks in one pass
+    (16, 32, False, "decoder", 2),  # fast mode, more than four chunks: packing + decoder kernel
+])
+def test_bench_pq_route_matches_the_library_routing(nqry, nq, exact, route, launches):
+    """bench.py's kernel-launch claim follows csrc/pq_adc.cu's routing (M=16, K=256, dsub=8)."""
+    import bench
+    assert bench.pq_route(nqry, nq, 16, 256, 8, exact) == route
+    assert bench.pq_score_launches(nqry, nq, 16, 256, 8, exact) == launches
+
+
+def test_bench_residual_launches_match_the_library_routing():
+    """Up to four query chunks: the token-rows kernel (+ the chunk sum for > 32-token queries);
+    more: packing + the dense kernel's residual decoder warps."""
+    import bench
+    assert bench.res_score_launches(1, 32) == 1
+    assert bench.res_score_launches(2, 64) == 2
+    assert bench.res_score_launches(5, 32) == 2
